@@ -1,0 +1,380 @@
+// C-ABI entry points for GEMM, batched GEMM and SYRK, plus the fp32 (3xTF32)
+// operand split kernel and the K == 0 scale kernel.
+#include <algorithm>
+#include <string>
+
+#include "gemm_sm100.cuh"
+#include "runtime.hpp"
+
+namespace tb {
+
+// ---------------------------------------------------------------------------
+// 3xTF32 split: hi = tf32 round-to-nearest-even of x (low 13 mantissa bits
+// zero), lo = x - hi (exact in fp32). Reads the logical R x K operand with
+// arbitrary strides (rs, ks) and writes K-major hi / lo planes (R x ldo),
+// zero in the K padding. 32 x 32 tiles through shared memory so both the
+// strided read and the K-contiguous write are coalesced.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tf32_rne(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
+  const uint32_t lsb = (u >> 13) & 1u;
+  u = (u + 0xFFFu + lsb) & 0xFFFFE000u;
+  return __uint_as_float(u);
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ X, long long rs, long long ks,
+                                  long long bs, int R, int K, int ldo, long long obs,
+                                  float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int k0 = blockIdx.x * 32;
+  const int r0 = blockIdx.y * 32;
+  const long long b = blockIdx.z;
+  const float* Xb = X + b * bs;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  if (ks == 1) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      tile[i][tx] = (r < R && k < K) ? __ldg(Xb + r * rs + k) : 0.0f;
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      tile[tx][i] = (r < R && k < K) ? __ldg(Xb + r * rs + k * ks) : 0.0f;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, k = k0 + tx;
+    if (r < R && k < ldo) {
+      const float x = tile[i][tx];
+      const float h = tf32_rne(x);
+      const long long o = b * obs + static_cast<long long>(r) * ldo + k;
+      hi[o] = h;
+      lo[o] = ((__float_as_uint(x) & 0x7F800000u) == 0x7F800000u) ? 0.0f : x - h;
+    }
+  }
+}
+
+// D = beta * C (K == 0): an empty sum times alpha is zero.
+__global__ void scale_c_kernel(int out_kind, long long batch, int M, int N, float beta,
+                               const void* C, long long ldc, long long strideC, void* D,
+                               long long ldd, long long strideD) {
+  const long long total = batch * static_cast<long long>(M) * N;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long b = i / (static_cast<long long>(M) * N);
+    const long long rc = i - b * M * static_cast<long long>(N);
+    const int r = static_cast<int>(rc / N), c = static_cast<int>(rc % N);
+    float v = 0.0f;
+    if (C && beta != 0.0f) v = beta * load_c(C, out_kind, b * strideC + r * ldc + c);
+    store_d(D, out_kind, b * strideD + r * ldd + c, v);
+  }
+}
+
+namespace {
+
+CUtensorMapDataType map_dtype(int dtype) {
+  switch (dtype) {
+    case TRNBLAS_BF16:
+      return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case TRNBLAS_F16:
+      return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default:
+      return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+template <int KIND, int BN, int STAGES>
+int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+                const CUtensorMap& b1, GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<KIND, BN>;
+  constexpr int smem = STAGES * Cfg::STAGE_BYTES + 1024 + 256;
+  auto kern = gemm_sm100_kernel<KIND, BN, STAGES>;
+  static bool attr_set[64] = {};  // the attribute is set per device
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int grid = static_cast<int>(std::min<long long>(p.num_tiles, num_sms()));
+  kern<<<grid, 192, smem, stream>>>(a0, a1, b0, b1, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
+  return TRNBLAS_OK;
+}
+
+bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBLAS_F16; }
+
+// Bytes of one fp32 split plane (R x Kp) for `nb` batch entries, 256-aligned.
+size_t plane_bytes(long long nb, long long R, long long K) {
+  const long long kp = round_up(std::max<long long>(K, 1), 4);
+  return static_cast<size_t>(round_up(nb * R * kp * 4, 256));
+}
+
+int check_dims(long long batch, long long M, long long N, long long K) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) {
+    set_error("negative size");
+    return TRNBLAS_ERR_ARG;
+  }
+  const long long lim = (1ll << 31) - 1;
+  if (M > lim || N > lim || K > lim || batch > 65535ll * 65535ll) {
+    set_error("size exceeds the 2^31-1 element limit per dimension");
+    return TRNBLAS_ERR_ARG;
+  }
+  return TRNBLAS_OK;
+}
+
+int launch_split(const float* X, long long rs, long long ks, long long bs, long long nb,
+                 long long R, long long K, float* hi, float* lo, cudaStream_t stream) {
+  const long long kp = round_up(std::max<long long>(K, 1), 4);
+  dim3 grid(static_cast<unsigned>(ceil_div(kp, 32)), static_cast<unsigned>(ceil_div(R, 32)),
+            static_cast<unsigned>(nb));
+  if (grid.y > 65535 || grid.z > 65535) {
+    set_error("split grid too large");
+    return TRNBLAS_ERR_ARG;
+  }
+  split_tf32_kernel<<<grid, dim3(32, 8), 0, stream>>>(X, rs, ks, bs, static_cast<int>(R),
+                                                      static_cast<int>(K),
+                                                      static_cast<int>(kp), R * kp, hi, lo);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "split kernel launch");
+  return TRNBLAS_OK;
+}
+
+// Pick BN for the bf16/fp16 GEMM: 256 unless 128 balances the waves better.
+int pick_bn(long long batch, long long M, long long N) {
+  if (N <= 128) return 128;
+  const long long sms = num_sms();
+  auto eff = [&](long long bn, double tile_eff) {
+    const long long tiles = batch * ceil_div(M, 128) * ceil_div(N, bn);
+    const long long waves = ceil_div(tiles, sms);
+    const double fill = static_cast<double>(tiles) / static_cast<double>(waves * sms);
+    const double ncover = static_cast<double>(N) / static_cast<double>(ceil_div(N, bn) * bn);
+    return fill * ncover * tile_eff;
+  };
+  return eff(256, 1.0) >= eff(128, 0.85) ? 256 : 128;
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+size_t trnblas_gemm_workspace_size(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                   int64_t strideA, int64_t strideB) {
+  if (dtype != TRNBLAS_F32 || batch <= 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  const long long na = strideA ? batch : 1, nbb = strideB ? batch : 1;
+  return 2 * plane_bytes(na, M, K) + 2 * plane_bytes(nbb, N, K);
+}
+
+int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                 const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                 int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                 int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
+                 void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (int rc = check_dims(batch, M, N, K)) return rc;
+  if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
+    set_error("trnblas_gemm: dtype must be F32, BF16 or F16");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (batch == 0 || M == 0 || N == 0) return TRNBLAS_OK;
+  if (!D || (K > 0 && (!A || !B))) {
+    set_error("trnblas_gemm: NULL operand");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (ldd < N || (C && beta != 0.0f && ldc < N)) {
+    set_error("trnblas_gemm: ldc/ldd smaller than N");
+    return TRNBLAS_ERR_ARG;
+  }
+  int* status = status_word();
+  if (!status) return TRNBLAS_ERR_CUDA;
+  const int out_kind = dtype == TRNBLAS_F32 ? kOutF32 : dtype == TRNBLAS_BF16 ? kOutBF16 : kOutF16;
+  if (K == 0) {
+    const long long total = batch * M * N;
+    const int blocks = static_cast<int>(std::min<long long>(ceil_div(total, 256), 4096));
+    scale_c_kernel<<<blocks, 256, 0, stream>>>(out_kind, batch, static_cast<int>(M),
+                                               static_cast<int>(N), beta, C, ldc, strideC, D,
+                                               ldd, strideD);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "scale kernel launch");
+  }
+
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.batch = static_cast<int>(batch);
+  p.mode = kModeGemm;
+  p.out_kind = out_kind;
+  p.c_mode = (C && beta != 0.0f) ? kCRow : kCNone;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.C = C;
+  p.ldc = ldc;
+  p.strideC = strideC;
+  p.D = D;
+  p.ldd = ldd;
+  p.strideD = strideD;
+  p.group_m = 16;
+  p.status = status;
+  p.timeout_ns = wait_timeout_ns();
+  const bool a_b = strideA != 0 && batch > 1;
+  const bool b_b = strideB != 0 && batch > 1;
+  p.a_batched = a_b;
+  p.b_batched = b_b;
+  const long long nba = a_b ? batch : 1, nbb = b_b ? batch : 1;
+
+  CUtensorMap ma0, ma1, mb0, mb1;
+  if (dtype == TRNBLAS_F32) {
+    const size_t need = trnblas_gemm_workspace_size(dtype, batch, M, N, K, strideA, strideB);
+    if (!workspace || workspace_bytes < need) {
+      set_error("trnblas_gemm: fp32 needs " + std::to_string(need) + " workspace bytes");
+      return TRNBLAS_ERR_WORKSPACE;
+    }
+    const long long kp = round_up(K, 4);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* ahi = reinterpret_cast<float*>(ws);
+    float* alo = reinterpret_cast<float*>(ws + plane_bytes(nba, M, K));
+    float* bhi = reinterpret_cast<float*>(ws + 2 * plane_bytes(nba, M, K));
+    float* blo = reinterpret_cast<float*>(ws + 2 * plane_bytes(nba, M, K) + plane_bytes(nbb, N, K));
+    const float* Af = static_cast<const float*>(A);
+    const float* Bf = static_cast<const float*>(B);
+    // op(A)(m, k) and op(B)^T(n, k) strides
+    const long long ars = transA ? 1 : lda, aks = transA ? lda : 1;
+    const long long brs = transB ? ldb : 1, bks = transB ? 1 : ldb;
+    if (int rc = launch_split(Af, ars, aks, a_b ? strideA : 0, nba, M, K, ahi, alo, stream)) return rc;
+    if (int rc = launch_split(Bf, brs, bks, b_b ? strideB : 0, nbb, N, K, bhi, blo, stream)) return rc;
+    const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (!encode_map_3d(&ma0, dt, 4, ahi, K, M, nba, kp, M * kp, 32, 128) ||
+        !encode_map_3d(&ma1, dt, 4, alo, K, M, nba, kp, M * kp, 32, 128) ||
+        !encode_map_3d(&mb0, dt, 4, bhi, K, N, nbb, kp, N * kp, 32, 128) ||
+        !encode_map_3d(&mb1, dt, 4, blo, K, N, nbb, kp, N * kp, 32, 128))
+      return TRNBLAS_ERR_ALIGN;
+    p.a_mn = 0;
+    p.b_mn = 0;
+    p.in_fmt = kFmtTF32;
+    p.tiles_m = static_cast<int>(ceil_div(M, 128));
+    p.tiles_n = static_cast<int>(ceil_div(N, 128));
+    p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+    return launch_gemm<kTF32x3, 128, 3>(ma0, ma1, mb0, mb1, p, stream);
+  }
+
+  // bf16 / fp16: operands straight from their own layout.
+  const int bn = pick_bn(batch, M, N);
+  const auto dt = map_dtype(dtype);
+  p.a_mn = transA ? 1 : 0;   // A stored K x M: M contiguous
+  p.b_mn = transB ? 0 : 1;   // B stored K x N: N contiguous
+  p.in_fmt = dtype == TRNBLAS_BF16 ? kFmtBF16 : kFmtF16;
+  const long long a_rows = transA ? K : M, a_cols = transA ? M : K;
+  const long long b_rows = transB ? N : K, b_cols = transB ? K : N;
+  if (lda < a_cols || ldb < b_cols) {
+    set_error("trnblas_gemm: lda/ldb smaller than the stored row length");
+    return TRNBLAS_ERR_ARG;
+  }
+  const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 8);
+  const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 8);
+  bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)
+                   : encode_map_3d(&ma0, dt, 2, A, K, M, nba, lda, sa2, 64, 128);
+  ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 2, B, N, K, nbb, ldb, sb2, 64, 64)
+                     : encode_map_3d(&mb0, dt, 2, B, K, N, nbb, ldb, sb2, 64, bn));
+  if (!ok) return TRNBLAS_ERR_ALIGN;
+  p.tiles_m = static_cast<int>(ceil_div(M, 128));
+  p.tiles_n = static_cast<int>(ceil_div(N, bn));
+  p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+  if (bn == 256) return launch_gemm<kF16, 256, 4>(ma0, ma0, mb0, mb0, p, stream);
+  return launch_gemm<kF16, 128, 6>(ma0, ma0, mb0, mb0, p, stream);
+}
+
+size_t trnblas_syrk_workspace_size(int dtype, int64_t n, int64_t k) {
+  if (dtype != TRNBLAS_F32 || n <= 0 || k <= 0) return 0;
+  return 2 * plane_bytes(1, n, k);
+}
+
+int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, int64_t lda,
+                 int trans, float beta, const void* C, int64_t ldc, int c_uplo, void* D,
+                 int64_t ldd, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (int rc = check_dims(1, n, n, k)) return rc;
+  if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
+    set_error("trnblas_syrk: dtype must be F32, BF16 or F16");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (c_uplo < 0 || c_uplo > 2) {
+    set_error("trnblas_syrk: c_uplo must be 0, 1 (lower) or 2 (upper)");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (n == 0) return TRNBLAS_OK;
+  const bool use_c = C && beta != 0.0f && c_uplo != 0;
+  if (!D || (k > 0 && !A) || ldd < n || (use_c && ldc < n)) {
+    set_error("trnblas_syrk: NULL operand or leading dimension smaller than n");
+    return TRNBLAS_ERR_ARG;
+  }
+  int* status = status_word();
+  if (!status) return TRNBLAS_ERR_CUDA;
+  const int out_kind = dtype == TRNBLAS_F32 ? kOutF32 : dtype == TRNBLAS_BF16 ? kOutBF16 : kOutF16;
+  GemmParams p{};
+  p.M = static_cast<int>(n);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.batch = 1;
+  p.mode = kModeSyrk;
+  p.out_kind = out_kind;
+  p.c_mode = use_c ? (c_uplo == 1 ? kCRow : kCTrans) : kCNone;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.C = C;
+  p.ldc = ldc;
+  p.D = D;
+  p.ldd = ldd;
+  p.group_m = 16;
+  p.status = status;
+  p.timeout_ns = wait_timeout_ns();
+  p.tiles_m = p.tiles_n = static_cast<int>(ceil_div(n, 128));
+  p.num_tiles = p.tiles_m * (p.tiles_m + 1) / 2;
+  if (k == 0) {
+    // beta * sym(C) alone needs no tile walk; the Python layer forms it.
+    set_error("trnblas_syrk: k must be positive");
+    return TRNBLAS_ERR_ARG;
+  }
+  CUtensorMap ma0, ma1;
+  if (dtype == TRNBLAS_F32) {
+    const size_t need = trnblas_syrk_workspace_size(dtype, n, k);
+    if (!workspace || workspace_bytes < need) {
+      set_error("trnblas_syrk: fp32 needs " + std::to_string(need) + " workspace bytes");
+      return TRNBLAS_ERR_WORKSPACE;
+    }
+    const long long kp = round_up(k, 4);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* ahi = reinterpret_cast<float*>(ws);
+    float* alo = reinterpret_cast<float*>(ws + plane_bytes(1, n, k));
+    const long long rs = trans ? 1 : lda, ks = trans ? lda : 1;
+    if (int rc = launch_split(static_cast<const float*>(A), rs, ks, 0, 1, n, k, ahi, alo, stream))
+      return rc;
+    const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (!encode_map_3d(&ma0, dt, 4, ahi, k, n, 1, kp, n * kp, 32, 128) ||
+        !encode_map_3d(&ma1, dt, 4, alo, k, n, 1, kp, n * kp, 32, 128))
+      return TRNBLAS_ERR_ALIGN;
+    p.in_fmt = kFmtTF32;
+    return launch_gemm<kTF32x3, 128, 3>(ma0, ma1, ma0, ma1, p, stream);
+  }
+  const auto dt = map_dtype(dtype);
+  p.a_mn = p.b_mn = trans ? 1 : 0;
+  p.in_fmt = dtype == TRNBLAS_BF16 ? kFmtBF16 : kFmtF16;
+  const long long rows = trans ? k : n, cols = trans ? n : k;
+  if (lda < cols) {
+    set_error("trnblas_syrk: lda smaller than the stored row length");
+    return TRNBLAS_ERR_ARG;
+  }
+  const long long s2 = round_up(lda * rows, 8);
+  const bool ok = trans ? encode_map_3d(&ma0, dt, 2, A, n, k, 1, lda, s2, 64, 64)
+                        : encode_map_3d(&ma0, dt, 2, A, k, n, 1, lda, s2, 64, 128);
+  if (!ok) return TRNBLAS_ERR_ALIGN;
+  return launch_gemm<kF16, 128, 6>(ma0, ma0, ma0, ma0, p, stream);
+}
+
+}  // extern "C"

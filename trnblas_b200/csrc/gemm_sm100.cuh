@@ -1,0 +1,428 @@
+// Warp-specialised, persistent tcgen05 GEMM engine for sm_100a.
+//
+// One CTA per SM walks output tiles with a static stride. Six warps:
+//   warp 0      TMA producer (one elected thread) filling a STAGES-deep ring;
+//   warp 1      TMEM owner + MMA issuer (one elected thread);
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, alpha/beta and the
+//               C operand fused, converted and stored straight to global.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile t overlaps the main loop of tile t+1.
+//
+// Operand kinds:
+//   kF16   bf16 / fp16 operands, kind::f16, fp32 accumulate, one product.
+//          Each operand is K-major or MN-major (the layout a transposed or
+//          row-major B gives) -- no transposed copies are made.
+//   kTF32x3 fp32 API: operands pre-split into (hi, lo) with hi = tf32(x) and
+//          lo = x - hi; acc += lo*hi + hi*lo + hi*hi on kind::tf32, which holds
+//          about 2^-22 relative error per product (fp32-class). K-major only.
+//
+// Modes:
+//   GEMM  tiles of D[b] = alpha * op(A[b]) op(B[b]) + beta * C[b], batched
+//         over a grid dimension folded into the tile index;
+//   SYRK  lower-triangle tiles only (BM == BN); each value v(r,c), r >= c, is
+//         stored at (r,c) and mirrored to (c,r), so the full symmetric result
+//         is exactly symmetric and the upper tiles are never computed.
+#pragma once
+
+#include "common.cuh"
+
+namespace tb {
+
+enum GemmKind : int { kF16 = 0, kTF32x3 = 1 };
+enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
+enum GemmMode : int { kModeGemm = 0, kModeSyrk = 1 };
+// How the epilogue reads C: not at all, C[r][c], or (SYRK, upper-triangle
+// storage) C[c][r] for the lower element (r, c).
+enum CMode : int { kCNone = 0, kCRow = 1, kCTrans = 2 };
+
+struct GemmParams {
+  int M, N, K;
+  int batch;
+  int a_batched, b_batched;  // TMA batch coordinate = batch index, or 0 (broadcast)
+  int a_mn, b_mn;            // operand smem layout: 0 = K-major, 1 = MN-major
+  int mode;                  // GemmMode
+  int out_kind;              // OutKind
+  int in_fmt;                // kFmtBF16 / kFmtF16 / kFmtTF32 (instruction descriptor)
+  int c_mode;                // CMode
+  float alpha, beta;
+  const void* C;
+  long long ldc, strideC;
+  void* D;
+  long long ldd, strideD;
+  int tiles_m, tiles_n, num_tiles;
+  int group_m;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+template <int KIND, int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int ESIZE = (KIND == kF16) ? 2 : 4;
+  static constexpr int BK = 128 / ESIZE;  // one 128-byte swizzle row of K
+  static constexpr int NPARTS = (KIND == kTF32x3) ? 2 : 1;  // hi/lo
+  static constexpr int A_TILE = BM * 128;  // bytes of one A part
+  static constexpr int B_TILE = BN * 128;
+  static constexpr int STAGE_BYTES = NPARTS * (A_TILE + B_TILE);
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+};
+
+__device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz, int& mb,
+                                            int& nb) {
+  if (p.mode == kModeSyrk) {
+    // lower triangle, row-major over (mb, nb <= mb)
+    int m = static_cast<int>((sqrtf(8.0f * static_cast<float>(t) + 1.0f) - 1.0f) * 0.5f);
+    while (m * (m + 1) / 2 > t) --m;
+    while ((m + 1) * (m + 2) / 2 <= t) ++m;
+    bz = 0;
+    mb = m;
+    nb = t - m * (m + 1) / 2;
+    return;
+  }
+  const int per_batch = p.tiles_m * p.tiles_n;
+  bz = t / per_batch;
+  int r = t - bz * per_batch;
+  const int band = p.group_m * p.tiles_n;
+  const int g = r / band;
+  const int first_m = g * p.group_m;
+  int gsz = p.tiles_m - first_m;
+  if (gsz > p.group_m) gsz = p.group_m;
+  const int rr = r - g * band;
+  mb = first_m + rr % gsz;
+  nb = rr / gsz;
+}
+
+__device__ __forceinline__ float load_c(const void* C, int out_kind, long long idx) {
+  if (out_kind == kOutF32) return __ldg(reinterpret_cast<const float*>(C) + idx);
+  if (out_kind == kOutBF16)
+    return __bfloat162float(
+        __ushort_as_bfloat16(__ldg(reinterpret_cast<const unsigned short*>(C) + idx)));
+  return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(C) + idx)));
+}
+
+__device__ __forceinline__ void store_d(void* D, int out_kind, long long idx, float v) {
+  if (out_kind == kOutF32) {
+    reinterpret_cast<float*>(D)[idx] = v;
+  } else if (out_kind == kOutBF16) {
+    reinterpret_cast<__nv_bfloat16*>(D)[idx] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(D)[idx] = __float2half_rn(v);
+  }
+}
+
+// Epilogue for one 32-column chunk held by this thread: row r (global), columns
+// c0 .. c0+31 (global), accumulator values v[32].
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int r, int c0,
+                                               const uint32_t (&v)[32], bool diag_tile) {
+  const long long dbase = static_cast<long long>(bz) * p.strideD;
+  const long long cbase = static_cast<long long>(bz) * p.strideC;
+  const bool has_c = (p.c_mode != kCNone) && (p.beta != 0.0f);
+  if (p.mode == kModeGemm) {
+    if (r >= p.M) return;
+    float out[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) out[j] = p.alpha * u2f(v[j]);
+    const bool full = (c0 + 32 <= p.N);
+    if (has_c) {
+      const long long crow = cbase + static_cast<long long>(r) * p.ldc;
+      if (full && p.out_kind == kOutF32 && (p.ldc % 4 == 0) &&
+          ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((cbase & 3) == 0)) {
+        const float4* cp = reinterpret_cast<const float4*>(
+            reinterpret_cast<const float*>(p.C) + crow + c0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 c4 = __ldg(cp + j);
+          out[4 * j + 0] += p.beta * c4.x;
+          out[4 * j + 1] += p.beta * c4.y;
+          out[4 * j + 2] += p.beta * c4.z;
+          out[4 * j + 3] += p.beta * c4.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < p.N) out[j] += p.beta * load_c(p.C, p.out_kind, crow + c0 + j);
+      }
+    }
+    const long long drow = dbase + static_cast<long long>(r) * p.ldd;
+    if (p.out_kind == kOutF32) {
+      float* dp = reinterpret_cast<float*>(p.D) + drow + c0;
+      if (full && (p.ldd % 4 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
+        float4* d4 = reinterpret_cast<float4*>(dp);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          d4[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < p.N) dp[j] = out[j];
+      }
+    } else {
+      unsigned short* dp = reinterpret_cast<unsigned short*>(p.D) + drow + c0;
+      if (full && (p.ldd % 8 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
+        uint4* d4 = reinterpret_cast<uint4*>(dp);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float lo = out[8 * j + 2 * h], hi = out[8 * j + 2 * h + 1];
+            if (p.out_kind == kOutBF16) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+              w[h] = *reinterpret_cast<uint32_t*>(&b2);
+            } else {
+              __half2 h2 = __floats2half2_rn(lo, hi);
+              w[h] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+          }
+          d4[j] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < p.N) store_d(p.D, p.out_kind, drow + c0 + j, out[j]);
+      }
+    }
+    return;
+  }
+  // SYRK: lower element (r, c) with r >= c, mirrored to (c, r).
+  const int n = p.M;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int c = c0 + j;
+    const bool keep = (r < n) && (c < n) && (!diag_tile || c <= r);
+    if (keep) {
+      float val = p.alpha * u2f(v[j]);
+      if (has_c) {
+        const long long ci = (p.c_mode == kCRow)
+                                 ? cbase + static_cast<long long>(r) * p.ldc + c
+                                 : cbase + static_cast<long long>(c) * p.ldc + r;
+        val += p.beta * load_c(p.C, p.out_kind, ci);
+      }
+      store_d(p.D, p.out_kind, dbase + static_cast<long long>(r) * p.ldd + c, val);
+      if (c != r) store_d(p.D, p.out_kind, dbase + static_cast<long long>(c) * p.ldd + r, val);
+    }
+  }
+}
+
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a0,
+                      const __grid_constant__ CUtensorMap map_a1,
+                      const __grid_constant__ CUtensorMap map_b0,
+                      const __grid_constant__ CUtensorMap map_b1, const GemmParams p) {
+  using Cfg = GemmCfg<KIND, BN>;
+  constexpr int BM = Cfg::BM;
+  constexpr int BK = Cfg::BK;
+  constexpr uint32_t STAGE_BYTES = Cfg::STAGE_BYTES;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Abort ab{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_a0);
+    tma_prefetch_desc(&map_b0);
+    if (KIND == kTF32x3) {
+      tma_prefetch_desc(&map_a1);
+      tma_prefetch_desc(&map_b1);
+    }
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    // armed-but-unobserved stages (for the drain on abort)
+    bool aborted = false;
+    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x) {
+      int bz, mb, nb;
+      decode_tile(p, t, bz, mb, nb);
+      const int m0 = mb * BM;
+      const int n0 = nb * ((p.mode == kModeSyrk) ? BM : BN);
+      const int za = p.a_batched ? bz : 0;
+      const int zb = p.b_batched ? bz : 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
+          aborted = true;
+          break;
+        }
+        uint8_t* sa = smem + stage * STAGE_BYTES;
+        uint8_t* sb = sa + Cfg::NPARTS * Cfg::A_TILE;
+        mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+        const int k0 = kb * BK;
+        if (KIND == kF16) {
+          if (!p.a_mn) {
+            tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d(sa + j * (64 * 128), &map_a0, &full_bar[stage], m0 + 64 * j, k0, za);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sb, &map_b0, &full_bar[stage], k0, n0, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(sb + j * (64 * 128), &map_b0, &full_bar[stage], n0 + 64 * j, k0, zb);
+          }
+        } else {
+          tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
+          tma_load_3d(sa + Cfg::A_TILE, &map_a1, &full_bar[stage], k0, m0, za);
+          tma_load_3d(sb, &map_b0, &full_bar[stage], k0, n0, zb);
+          tma_load_3d(sb + Cfg::B_TILE, &map_b1, &full_bar[stage], k0, n0, zb);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (aborted || ab.raised()) {
+      // Let copies already issued land before the CTA exits: wait (bounded)
+      // for the most recent STAGES armed phases.
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < STAGES; ++i) {
+        if (s == 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        } else {
+          --s;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], ph)) {
+          if (globaltimer_ns() - t0 > 50000000ull) break;  // 50 ms
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc_v =
+        idesc(kAccF32, p.in_fmt, p.in_fmt, p.a_mn, p.b_mn, BM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool aborted = false;
+    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t accph = (it >> 1) & 1;
+      if (!mbar_wait(&acce_bar[acc], accph ^ 1u, ab, kTimeoutAccEmpty)) {
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+        const uint32_t sb = sa + Cfg::NPARTS * Cfg::A_TILE;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc_in = (kb | kk) != 0;
+          if (KIND == kF16) {
+            const uint64_t ad = p.a_mn ? sdesc_sw128(sa + kk * 2048, 64 * 128, 1024)
+                                       : sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = p.b_mn ? sdesc_sw128(sb + kk * 2048, 64 * 128, 1024)
+                                       : sdesc_sw128(sb + kk * 32, 16, 1024);
+            mma_f16(d_tmem, ad, bd, idesc_v, acc_in);
+          } else {
+            const uint64_t ah = sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t al = sdesc_sw128(sa + Cfg::A_TILE + kk * 32, 16, 1024);
+            const uint64_t bh = sdesc_sw128(sb + kk * 32, 16, 1024);
+            const uint64_t bl = sdesc_sw128(sb + Cfg::B_TILE + kk * 32, 16, 1024);
+            mma_tf32(d_tmem, al, bh, idesc_v, acc_in);  // small terms first
+            mma_tf32(d_tmem, ah, bl, idesc_v, 1u);
+            mma_tf32(d_tmem, ah, bh, idesc_v, 1u);
+          }
+        }
+        tc_commit(&empty_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (aborted) break;
+      tc_commit(&accf_bar[acc]);
+    }
+    // Every MMA this thread issued must finish before TMEM is released.
+    tc_commit(drain_bar);
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(drain_bar, 0)) {
+      if (globaltimer_ns() - t0 > 100000000ull) {  // 100 ms
+        ab.raise(kTimeoutDrain);
+        break;
+      }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = 32 * q + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t accph = (it >> 1) & 1;
+      if (!mbar_wait(&accf_bar[acc], accph, ab, kTimeoutAccFull)) break;
+      tc_fence_after();
+      int bz, mb, nb;
+      decode_tile(p, t, bz, mb, nb);
+      const int r = mb * BM + row_in_tile;
+      const int ncol = (p.mode == kModeSyrk) ? BM : BN;
+      const int n0 = nb * ncol;
+      const bool diag = (p.mode == kModeSyrk) && (mb == nb);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < ncol / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tbase + c * 32, v);
+        tmem_ld_wait();
+        if (n0 + c * 32 < ((p.mode == kModeSyrk) ? p.M : p.N))
+          epilogue_chunk(p, bz, r, n0 + c * 32, v, diag);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace tb

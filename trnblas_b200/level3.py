@@ -1,0 +1,435 @@
+"""BLAS level 3 on B200: gemm, batched_gemm, syrk, gemm_fp64.
+
+Same signatures, argument meanings, return dtypes and exceptions as the
+reference's trnblas/level3.py (gemm :69-109, batched_gemm :112-134, gemm_fp64
+:137-193, syrk :243-295). Every float32 / bfloat16 / float16 product runs on
+the sm_100a tcgen05 kernels through the C ABI (`_native`); there is no routing
+table and no torch.matmul fallback for those dtypes. Host (CPU) tensors are
+uploaded to the current CUDA device, computed there, and the result comes back
+to the host, so a call keeps the reference's "result on the input's device"
+contract. Other dtypes (float64, complex, integer) have no kernel in the
+reference either; they run torch.matmul on the operands' device, as the
+reference's pytorch route does (trnblas/nki/dispatch.py:321-338).
+"""
+
+from __future__ import annotations
+
+import math
+import warnings
+
+import torch
+
+from . import _native as N
+from ._flags import trans_flag, uplo_flag
+
+# ── device placement ─────────────────────────────────────────────────────────
+
+
+def _cuda_device(*tensors: torch.Tensor) -> torch.device:
+    """The CUDA device the kernels run on for these operands."""
+    devs = {t.device for t in tensors if isinstance(t, torch.Tensor) and t.device.type == "cuda"}
+    if len(devs) > 1:
+        raise RuntimeError(f"trnblas_b200: operands on different CUDA devices: {sorted(map(str, devs))}")
+    if devs:
+        return devs.pop()
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            "trnblas_b200 runs on NVIDIA B200 (sm_100a); no CUDA device is available"
+        )
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _to(t, dev):
+    if t is None or not isinstance(t, torch.Tensor):
+        return t
+    if t.device == dev:
+        return t
+    return t.to(dev, non_blocking=t.device.type == "cpu" and t.is_pinned())
+
+
+# ── operand layout for the TMA path ─────────────────────────────────────────
+
+
+def _tma_operand(x: torch.Tensor, esize: int):
+    """(tensor, ld, transposed) for a 2-D logical operand x (rows x cols).
+
+    transposed=False: x[r, c] = t[r * ld + c] (row-major, cols contiguous);
+    transposed=True:  x[r, c] = t[c * ld + r] (t stores x^T row-major).
+    The 16-byte TMA rule needs ld * esize % 16 == 0 and a 16-byte aligned base;
+    otherwise a zero-padded row-major copy is made (small / ragged shapes only).
+    """
+    rows, cols = x.shape
+    q = 16 // esize
+    aligned = x.data_ptr() % 16 == 0
+    s0, s1 = x.stride()
+    if aligned and (s1 == 1 or cols == 1) and s0 % q == 0 and s0 >= cols and s0 > 0:
+        return x, s0, False
+    if aligned and (s0 == 1 or rows == 1) and s1 % q == 0 and s1 >= rows and s1 > 0:
+        return x, s1, True
+    ld = -(-max(cols, 1) // q) * q
+    buf = torch.zeros((rows, ld), dtype=x.dtype, device=x.device)
+    buf[:, :cols].copy_(x)
+    return buf, ld, False
+
+
+def _gemm2d(a: torch.Tensor, b: torch.Tensor, alpha: float, beta: float, C) -> torch.Tensor:
+    """alpha * a @ b (+ beta * C when C is a same-shape, same-dtype matrix) on the kernel."""
+    M, K = a.shape
+    K2, Nn = b.shape
+    if K != K2:
+        raise RuntimeError(f"mat1 and mat2 shapes cannot be multiplied ({M}x{K} and {K2}x{Nn})")
+    dev = a.device
+    out = torch.empty((M, Nn), dtype=a.dtype, device=dev)
+    if M == 0 or Nn == 0:
+        return out
+    code = N.dtype_code(a.dtype)
+    es = a.element_size()
+    if code == N.F32:
+        # The split pre-pass reads any unit-stride layout; no TMA constraints.
+        at, lda, ta = _f32_operand(a)
+        bt, ldb, tb = _f32_operand(b)
+    else:
+        # "transposed" storage of B means the tensor stores B^T (N x K) row-major.
+        at, lda, ta = _tma_operand(a, es)
+        bt, ldb, tb = _tma_operand(b, es)
+    c_arg, ldc = None, 0
+    if C is not None and beta != 0.0:
+        c_arg = C if C.stride(1) == 1 and C.stride(0) >= Nn else C.contiguous()
+        ldc = c_arg.stride(0)
+    ws_bytes = N.lib().trnblas_gemm_workspace_size(code, 1, M, Nn, K, 0, 0)
+    ws = N.workspace(ws_bytes, dev)
+    rc = N.lib().trnblas_gemm(
+        code, 1, M, Nn, K, float(alpha),
+        N.ptr(at), lda, 0, int(ta),
+        N.ptr(bt), ldb, 0, int(tb),
+        float(beta) if c_arg is not None else 0.0, N.ptr(c_arg), ldc, 0,
+        N.ptr(out), Nn, 0,
+        N.ptr(ws), ws_bytes, N.stream_ptr(dev),
+    )
+    N.check(rc, "trnblas_gemm")
+    return out
+
+
+def _fuse_c(C, beta: float, shape, dtype, dev) -> bool:
+    return (
+        C is not None
+        and beta != 0.0
+        and isinstance(C, torch.Tensor)
+        and tuple(C.shape) == tuple(shape)
+        and C.dtype == dtype
+        and C.device == dev
+    )
+
+
+def _add_c(result: torch.Tensor, beta: float, C) -> torch.Tensor:
+    """result + beta * C with torch broadcasting / promotion (non-fusable C)."""
+    if C is None or beta == 0.0:
+        return result
+    if (
+        isinstance(C, torch.Tensor)
+        and C.dtype == result.dtype
+        and torch.broadcast_shapes(result.shape, C.shape) == result.shape
+    ):
+        return result.add_(_to(C, result.device), alpha=beta)
+    return result + beta * _to(C, result.device)
+
+
+def _mixed_dtype_error(a: torch.Tensor, b: torch.Tensor):
+    raise RuntimeError(
+        f"expected m1 and m2 to have the same dtype, but got: {a.dtype} != {b.dtype}"
+    )
+
+
+# ── public API ───────────────────────────────────────────────────────────────
+
+
+def gemm(
+    alpha: float,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    beta: float = 0.0,
+    C: torch.Tensor | None = None,
+    transA: bool = False,
+    transB: bool = False,
+) -> torch.Tensor:
+    """General matrix multiply: C = alpha * op(A) @ op(B) + beta * C.
+
+    op(X) = X, or X^T when trans (for >= 3-D operands the last two dimensions,
+    as in `batched_gemm`). alpha, beta and the C operand are fused into the
+    kernel epilogue when C is a same-shape, same-dtype matrix; a broadcasting
+    C is added afterwards with torch semantics. beta == 0 never reads C.
+    fp32 runs as 3xTF32 (fp32-class error), bf16/fp16 natively with fp32
+    accumulation; the result has the input dtype and a fresh buffer.
+    """
+    transA, transB = trans_flag(transA, "transA"), trans_flag(transB, "transB")
+    a = A.mT if transA and A.dim() >= 2 else A
+    b = B.mT if transB and B.dim() >= 2 else B
+    if a.dim() >= 3 or b.dim() >= 3:
+        return _batched(alpha, a, b, beta, C)
+    return _gemm_public(alpha, a, b, beta, C)
+
+
+def _gemm_public(alpha, a, b, beta, C):
+    if a.dtype != b.dtype:
+        _mixed_dtype_error(a, b)
+    if a.dtype not in N.KERNEL_DTYPES:
+        r = torch.matmul(a, b)
+        r = alpha * r
+        return r + beta * C if (C is not None and beta != 0.0) else r
+    home = a.device
+    dev = _cuda_device(a, b, C)
+    a2, b2 = _to(a, dev), _to(b, dev)
+    squeeze = []
+    if a2.dim() == 1:
+        a2 = a2.unsqueeze(0)
+        squeeze.append(-2)
+    if b2.dim() == 1:
+        b2 = b2.unsqueeze(1)
+        squeeze.append(-1)
+    if a2.dim() != 2 or b2.dim() != 2:
+        raise RuntimeError("gemm: operands must be 1-D, 2-D or batched")
+    shape = (a2.shape[0], b2.shape[1])
+    Cd = _to(C, dev)
+    fuse = not squeeze and _fuse_c(Cd, beta, shape, a.dtype, dev)
+    r = _gemm2d(a2, b2, alpha, beta if fuse else 0.0, Cd if fuse else None)
+    for d in squeeze:
+        r = r.squeeze(d)
+    if not fuse:
+        r = _add_c(r, beta, Cd)
+    return r.to(home) if home != dev else r
+
+
+def _flat_batch(x: torch.Tensor, batch: tuple, esize: int, f32: bool):
+    """(tensor, ld, transposed, batch_stride) with x expanded to `batch`.
+
+    A broadcast operand keeps batch stride 0 (one matrix read for all);
+    otherwise the batch dims must collapse to one stride, else a copy is made.
+    """
+    rows, cols = x.shape[-2:]
+    nb = math.prod(batch)
+    xb = x.expand(*batch, rows, cols)
+    bstr = [s for s, n in zip(xb.stride()[:-2], batch, strict=True) if n > 1]
+    if nb <= 1 or all(s == 0 for s in bstr):
+        m, ld, tr = (_tma_operand(xb.reshape(-1, rows, cols)[0], esize) if not f32 else _f32_operand(xb.reshape(-1, rows, cols)[0]))
+        return m, ld, tr, 0
+    try:
+        flat = xb.view(nb, rows, cols)
+    except RuntimeError:
+        flat = xb.reshape(nb, rows, cols).contiguous()
+    s0 = flat.stride(0)
+    m2 = flat[0]
+    if f32:
+        m, ld, tr = _f32_operand(m2)
+        if m is not m2:
+            flat = flat.contiguous()
+            return flat, cols, False, flat.stride(0)
+        return flat, ld, tr, s0
+    q = 16 // esize
+    m, ld, tr = _tma_operand(m2, esize)
+    if m is m2 and s0 % q == 0 and flat.data_ptr() % 16 == 0:
+        return flat, ld, tr, s0
+    ldp = -(-max(cols, 1) // q) * q
+    buf = torch.zeros((nb, rows, ldp), dtype=x.dtype, device=x.device)
+    buf[:, :, :cols].copy_(flat)
+    return buf, ldp, False, rows * ldp
+
+
+def _f32_operand(x: torch.Tensor):
+    """(tensor, ld, transposed) for the fp32 split pre-pass (any unit-stride layout)."""
+    rows, cols = x.shape
+    s0, s1 = x.stride()
+    if s1 == 1 or cols == 1:
+        return x, max(s0, cols, 1), False
+    if s0 == 1 or rows == 1:
+        return x, max(s1, rows, 1), True
+    c = x.contiguous()
+    return c, max(cols, 1), False
+
+
+def _batched(alpha, a, b, beta, C):
+    if a.dtype != b.dtype:
+        _mixed_dtype_error(a, b)
+    if a.dim() < 2 or b.dim() < 2 or a.dtype not in N.KERNEL_DTYPES:
+        r = alpha * torch.matmul(a, b)
+        return r + beta * C if (C is not None and beta != 0.0) else r
+    batch = tuple(torch.broadcast_shapes(a.shape[:-2], b.shape[:-2]))
+    M, K = a.shape[-2:]
+    K2, Nn = b.shape[-2:]
+    if K != K2:
+        raise RuntimeError(
+            f"Expected size for first two dimensions of batch2 tensor to be: [{math.prod(batch)}, {K}] "
+            f"but got: [{math.prod(batch)}, {K2}]."
+        )
+    home = a.device
+    dev = _cuda_device(a, b, C)
+    a2, b2 = _to(a, dev), _to(b, dev)
+    nb = math.prod(batch)
+    out = torch.empty((*batch, M, Nn), dtype=a.dtype, device=dev)
+    Cd = _to(C, dev)
+    fuse = _fuse_c(Cd, beta, out.shape, a.dtype, dev)
+    if nb == 0 or M == 0 or Nn == 0:
+        r = out
+    else:
+        code = N.dtype_code(a.dtype)
+        es = a.element_size()
+        f32 = code == N.F32
+        at, lda, ta, sa = _flat_batch(a2, batch, es, f32)
+        bt, ldb, tb, sb = _flat_batch(b2, batch, es, f32)
+        c_arg, ldc, sc = None, 0, 0
+        if fuse:
+            c_arg = Cd.reshape(nb, M, Nn)
+            if not (c_arg.stride(2) == 1 and c_arg.stride(1) >= Nn):
+                c_arg = c_arg.contiguous()
+            ldc, sc = c_arg.stride(1), c_arg.stride(0)
+        ws_bytes = N.lib().trnblas_gemm_workspace_size(code, nb, M, Nn, K, sa, sb)
+        ws = N.workspace(ws_bytes, dev)
+        rc = N.lib().trnblas_gemm(
+            code, nb, M, Nn, K, float(alpha),
+            N.ptr(at), lda, sa, int(ta),
+            N.ptr(bt), ldb, sb, int(tb),
+            float(beta) if fuse else 0.0, N.ptr(c_arg), ldc, sc,
+            N.ptr(out), Nn, M * Nn,
+            N.ptr(ws), ws_bytes, N.stream_ptr(dev),
+        )
+        N.check(rc, "trnblas_gemm (batched)")
+        r = out
+    if not fuse:
+        r = _add_c(r, beta, Cd)
+    return r.to(home) if home != dev else r
+
+
+def batched_gemm(
+    alpha: float,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    beta: float = 0.0,
+    C: torch.Tensor | None = None,
+    transA: bool = False,
+    transB: bool = False,
+) -> torch.Tensor:
+    """Batched GEMM: C[i] = alpha * op(A[i]) @ op(B[i]) + beta * C[i].
+
+    torch.matmul batch semantics: batch dims broadcast, either operand may be
+    2-D. One kernel launch covers every batch entry (the batch index is folded
+    into the persistent tile walk); a broadcast operand is read, not copied.
+    """
+    transA, transB = trans_flag(transA, "transA"), trans_flag(transB, "transB")
+    a = A.transpose(-2, -1) if transA else A
+    b = B.transpose(-2, -1) if transB else B
+    if a.dim() == 2 and b.dim() == 2:
+        return _gemm_public(alpha, a, b, beta, C)
+    return _batched(alpha, a, b, beta, C)
+
+
+def _sym_from_triangle(C: torch.Tensor, uplo: str) -> torch.Tensor:
+    """The symmetric matrix stored in the `uplo` triangle of C."""
+    if uplo == "upper":
+        return torch.triu(C) + torch.triu(C, diagonal=1).mT
+    return torch.tril(C) + torch.tril(C, diagonal=-1).mT
+
+
+def _resolve_syrk_uplo(C: torch.Tensor, uplo: str) -> str:
+    """`uplo`, or the opposite triangle when only that one holds entries
+    (with a DeprecationWarning), as trnblas/level3.py:305-329."""
+    has_upper = bool(torch.triu(C, diagonal=1).ne(0).any())
+    has_lower = bool(torch.tril(C, diagonal=-1).ne(0).any())
+    other = "lower" if uplo == "upper" else "upper"
+    in_uplo, in_other = (has_upper, has_lower) if uplo == "upper" else (has_lower, has_upper)
+    if in_other and not in_uplo:
+        warnings.warn(
+            f"syrk: C stores its off-diagonal entries only in the {other} triangle "
+            f"but uplo={uplo!r}; using the {other} triangle. Pass uplo={other!r}. "
+            "Only the uplo triangle of C is referenced when both are stored.",
+            DeprecationWarning,
+            stacklevel=3,
+        )
+        return other
+    return uplo
+
+
+def _syrk_kernel(a_eff: torch.Tensor, alpha: float, beta: float, C, c_uplo: int) -> torch.Tensor:
+    """alpha * a_eff @ a_eff^T (+ beta * sym(C)) on the lower-triangle kernel."""
+    n, k = a_eff.shape
+    dev = a_eff.device
+    out = torch.empty((n, n), dtype=a_eff.dtype, device=dev)
+    if n == 0:
+        return out
+    code = N.dtype_code(a_eff.dtype)
+    if code == N.F32:
+        at, lda, tr = _f32_operand(a_eff)
+    else:
+        at, lda, tr = _tma_operand(a_eff, a_eff.element_size())
+    c_arg, ldc = None, 0
+    if C is not None and c_uplo:
+        c_arg = C if C.stride(1) == 1 and C.stride(0) >= n else C.contiguous()
+        ldc = c_arg.stride(0)
+    ws_bytes = N.lib().trnblas_syrk_workspace_size(code, n, k)
+    ws = N.workspace(ws_bytes, dev)
+    rc = N.lib().trnblas_syrk(
+        code, n, k, float(alpha), N.ptr(at), lda, int(tr),
+        float(beta) if c_arg is not None else 0.0, N.ptr(c_arg), ldc, c_uplo if c_arg is not None else 0,
+        N.ptr(out), n, N.ptr(ws), ws_bytes, N.stream_ptr(dev),
+    )
+    N.check(rc, "trnblas_syrk")
+    return out
+
+
+def _symmetrize(R: torch.Tensor) -> torch.Tensor:
+    return 0.5 * (R + R.mT)
+
+
+def syrk(
+    alpha: float,
+    A: torch.Tensor,
+    beta: float = 0.0,
+    C: torch.Tensor | None = None,
+    trans: bool = False,
+    uplo: str = "upper",
+) -> torch.Tensor:
+    """Symmetric rank-k update: alpha * A @ A^T + beta * C (trans=False) or
+    alpha * A^T @ A + beta * C (trans=True).
+
+    Returns the full symmetric matrix. Only the lower-triangle tiles are
+    computed on the tensor cores; each value is written to both triangles, so
+    the result is exactly symmetric. As in BLAS, only the `uplo` triangle of an
+    n x n C is referenced (a C stored only in the other triangle is still used,
+    with a DeprecationWarning). A broadcasting C is added and the sum
+    symmetrised.
+    """
+    trans = trans_flag(trans)
+    uplo = uplo_flag(uplo)
+    a_eff = A.mT if trans else A
+    if a_eff.dim() != 2:
+        raise ValueError(f"syrk expects a 2-D A, got shape {tuple(A.shape)}")
+    n, k = a_eff.shape
+    add = C is not None and beta != 0.0
+    if a_eff.dtype not in N.KERNEL_DTYPES:
+        S = torch.matmul(a_eff, a_eff.mT)
+        S = _symmetrize(S)
+        if add and C.dim() == 2 and tuple(C.shape) == (n, n):
+            return alpha * S + beta * _sym_from_triangle(C, _resolve_syrk_uplo(C, uplo))
+        R = alpha * S
+        return _symmetrize(R + beta * C) if add else R
+    home = A.device
+    dev = _cuda_device(A, C)
+    a2 = _to(a_eff, dev)
+    Cd = _to(C, dev)
+    square_c = add and Cd.dim() == 2 and tuple(Cd.shape) == (n, n)
+    if k == 0:
+        S = torch.zeros((n, n), dtype=a2.dtype, device=dev)
+        if square_c:
+            R = S + beta * _sym_from_triangle(Cd, _resolve_syrk_uplo(Cd, uplo))
+        else:
+            R = _symmetrize(S + beta * Cd) if add else S
+        return R.to(home) if home != dev else R
+    if square_c:
+        u = _resolve_syrk_uplo(Cd, uplo)
+        if Cd.dtype == a2.dtype:
+            R = _syrk_kernel(a2, alpha, beta, Cd, 1 if u == "lower" else 2)
+        else:
+            R = _syrk_kernel(a2, alpha, 0.0, None, 0) + beta * _sym_from_triangle(Cd, u)
+    else:
+        R = _syrk_kernel(a2, alpha, 0.0, None, 0)
+        if add:
+            R = _symmetrize(R + beta * Cd)
+    return R.to(home) if home != dev else R

@@ -119,10 +119,12 @@ TRNBLAS_API int trnblas_gemm_fp64(int64_t M, int64_t N, int64_t K, const double*
  * The Ozaki split alone (for parity checks): digits (slices, R, ldd) int8 and
  * exponents (R,) int32 of the R x K operand X (element (r, k) at
  * X[r * rs + k * ks]), scaled per row r. Digit d_s(r, k) is the reference's
- * digit of trnblas/ozaki.py:123-219 (split, per="row").
+ * digit of trnblas/ozaki.py:123-219 (split, per="row"). Needs
+ * 8 * R + 256 bytes of workspace.
  */
 TRNBLAS_API int trnblas_ozaki_split(int64_t R, int64_t K, const double* X, int64_t rs, int64_t ks,
-                        int slices, int8_t* digits, int64_t ldd, int32_t* exps, void* stream);
+                        int slices, int8_t* digits, int64_t ldd, int32_t* exps,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Bytes of workspace trnblas_pair_energy needs. */
 TRNBLAS_API size_t trnblas_pair_energy_workspace_size(int64_t nocc, int64_t nvir, int64_t naux,
@@ -133,9 +135,11 @@ TRNBLAS_API size_t trnblas_pair_energy_workspace_size(int64_t nocc, int64_t nvir
  * p = j (j + 1) / 2 + i in [pair_begin, pair_end):
  *   E = sum_p w_p sum_{a,b} T_ab (2 T_ab - T_ba) / (e_i + e_j - e_a - e_b),
  *   T = B_i B_j^T (nvir x nvir, contracted over naux), w_p = 1 (i == j) or 2.
- * B is (nocc, nvir, naux) fp32 contiguous, eps fp32. T is formed tile by tile
- * in TMEM by 3xTF32 and reduced in the epilogue; it never reaches HBM. The
- * fp64 result is written to *energy (device pointer). Deterministic.
+ * B is (nocc, nvir, naux) fp32 contiguous, eps fp32. B is split per row
+ * (i, a) into 3 int8 Ozaki digit planes; T is formed tile by tile from exact
+ * int32 diagonal sums in TMEM and reduced in the epilogue (fp64 partial sums);
+ * it never reaches HBM. The fp64 result is written to *energy (device
+ * pointer). Deterministic. naux <= 174762 (exact int32 sums).
  * Replaces trnblas/nki/dispatch.py:2537-2569 (nki_batched_pair_energy),
  * :2768-2795 (_nki_pair_energy_sym_impl), trnblas/nki/multicore.py:212-289
  * (sym_rows / aten_rows) and the NKI kernel dispatch.py:4900-5001

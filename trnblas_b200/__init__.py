@@ -10,7 +10,9 @@ from __future__ import annotations
 
 from . import _native
 from ._flags import diag_flag, side_flag, trans_flag, uplo_flag
-from .level3 import batched_gemm, gemm, syrk
+from . import energy, parallel
+from .energy import batched_pair_energy, nki_batched_pair_energy, pair_range_energy
+from .level3 import batched_gemm, gemm, gemm_fp64, syrk
 
 __version__ = "0.1.0"
 
@@ -41,10 +43,16 @@ def device_status(device=None) -> int:
 
 __all__ = [
     "batched_gemm",
+    "batched_pair_energy",
     "device_status",
     "diag_flag",
+    "energy",
     "gemm",
+    "gemm_fp64",
     "get_backend",
+    "nki_batched_pair_energy",
+    "pair_range_energy",
+    "parallel",
     "set_backend",
     "side_flag",
     "syrk",

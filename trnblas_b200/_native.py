@@ -45,7 +45,7 @@ _SIGNATURES = {
     "trnblas_gemm_fp64": (
         _i, [_i64, _i64, _i64, _p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _p, _sz, _p]
     ),
-    "trnblas_ozaki_split": (_i, [_i64, _i64, _p, _i64, _i64, _i, _p, _i64, _p, _p]),
+    "trnblas_ozaki_split": (_i, [_i64, _i64, _p, _i64, _i64, _i, _p, _i64, _p, _p, _sz, _p]),
     "trnblas_pair_energy_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "trnblas_pair_energy": (
         _i, [_i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _sz, _p]

@@ -257,6 +257,19 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// Generic K-major swizzled descriptor: layout 2 = 128B, 4 = 64B, 6 = 32B.
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr, uint32_t sbo_bytes,
+                                                 uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;  // LBO unused for swizzled K-major
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
+  return d;
+}
+enum : uint32_t { kSwz128 = 2, kSwz64 = 4, kSwz32 = 6 };
+
 // Instruction descriptor fields (kind::f16 / kind::tf32 / kind::i8).
 enum : uint32_t { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2, kFmtS8 = 1 };
 enum : uint32_t { kAccF32 = 1, kAccS32 = 2 };
@@ -272,5 +285,17 @@ __host__ __device__ constexpr uint32_t idesc(uint32_t acc_fmt, uint32_t a_fmt, u
 // Small numeric helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// 2^n as a double, exact, for n in [-1022, 1023].
+__device__ __forceinline__ double pow2d(int n) {
+  return __longlong_as_double(static_cast<long long>(n + 1023) << 52);
+}
+
+// v * 2^ex in two exact power-of-two steps (floor(ex/2), then the rest), so no
+// intermediate over/underflows for |ex| up to ~2000.
+__device__ __forceinline__ double scale2(double v, int ex) {
+  const int h = (ex >= 0) ? ex / 2 : -((-ex + 1) / 2);  // floor(ex / 2)
+  return (v * pow2d(h)) * pow2d(ex - h);
+}
 
 }  // namespace tb

@@ -5,8 +5,8 @@
 //   warp 1      TMEM owner + MMA issuer (one elected thread);
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator, alpha/beta and the
 //               C operand fused, converted and stored straight to global.
-// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
-// of tile t overlaps the main loop of tile t+1.
+// The accumulator is multi-buffered in TMEM so the epilogue of one tile (or K
+// chunk) overlaps the main loop of the next.
 //
 // Operand kinds:
 //   kF16   bf16 / fp16 operands, kind::f16, fp32 accumulate, one product.
@@ -64,7 +64,17 @@ struct GemmCfg {
   static constexpr int A_TILE = BM * 128;  // bytes of one A part
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE_BYTES = NPARTS * (A_TILE + B_TILE);
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  // K blocks accumulated in TMEM before the epilogue takes the partial sum.
+  // The tensor core accumulates fp32 with truncation, whose bias grows with
+  // the number of accumulations; for the fp32 API the partial sums of 128-wide
+  // K chunks are added in the epilogue with round-to-nearest instead, which
+  // bounds the relative error near 1e-6 at any K. bf16 / fp16 results round
+  // their output far above that bias, so they accumulate the whole K in TMEM.
+  static constexpr int CHUNK_KB = (KIND == kTF32x3) ? 4 : (1 << 30);
+  static constexpr int NBUF = (KIND == kTF32x3) ? 4 : 2;  // TMEM accumulator buffers
+  static constexpr int TMEM_COLS = (NBUF * BN <= 32) ? 32 : (NBUF * BN <= 64) ? 64 : (NBUF * BN <= 128) ? 128 : (NBUF * BN <= 256) ? 256 : 512;
+  static_assert(NBUF * BN <= 512, "TMEM holds 512 columns");
+  static_assert(KIND != kTF32x3 || BN == 128, "chunked epilogue keeps 128 columns in registers");
 };
 
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz, int& mb,
@@ -111,9 +121,9 @@ __device__ __forceinline__ void store_d(void* D, int out_kind, long long idx, fl
 }
 
 // Epilogue for one 32-column chunk held by this thread: row r (global), columns
-// c0 .. c0+31 (global), accumulator values v[32].
+// c0 .. c0+31 (global), accumulator values v[0..31].
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int r, int c0,
-                                               const uint32_t (&v)[32], bool diag_tile) {
+                                               const float* v, bool diag_tile) {
   const long long dbase = static_cast<long long>(bz) * p.strideD;
   const long long cbase = static_cast<long long>(bz) * p.strideC;
   const bool has_c = (p.c_mode != kCNone) && (p.beta != 0.0f);
@@ -121,7 +131,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int 
     if (r >= p.M) return;
     float out[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) out[j] = p.alpha * u2f(v[j]);
+    for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
     const bool full = (c0 + 32 <= p.N);
     if (has_c) {
       const long long crow = cbase + static_cast<long long>(r) * p.ldc;
@@ -191,7 +201,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int 
     const int c = c0 + j;
     const bool keep = (r < n) && (c < n) && (!diag_tile || c <= r);
     if (keep) {
-      float val = p.alpha * u2f(v[j]);
+      float val = p.alpha * v[j];
       if (has_c) {
         const long long ci = (p.c_mode == kCRow)
                                  ? cbase + static_cast<long long>(r) * p.ldc + c
@@ -220,9 +230,9 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
-  uint64_t* acce_bar = accf_bar + 2;        // [2]
-  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  uint64_t* accf_bar = empty_bar + STAGES;   // [NBUF]
+  uint64_t* acce_bar = accf_bar + Cfg::NBUF;  // [NBUF]
+  uint64_t* drain_bar = acce_bar + Cfg::NBUF; // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -235,7 +245,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < Cfg::NBUF; ++a) {
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], 4);
     }
@@ -330,52 +340,55 @@ __global__ void __launch_bounds__(192, 1)
         idesc(kAccF32, p.in_fmt, p.in_fmt, p.a_mn, p.b_mn, BM, BN);
     int stage = 0;
     uint32_t phase = 0;
-    int it = 0;
+    int gc = 0;  // accumulation chunks issued by this CTA
     bool aborted = false;
-    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t accph = (it >> 1) & 1;
-      if (!mbar_wait(&acce_bar[acc], accph ^ 1u, ab, kTimeoutAccEmpty)) {
-        aborted = true;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x) {
+      for (int kb0 = 0; kb0 < num_kb && !aborted; kb0 += Cfg::CHUNK_KB, ++gc) {
+        const int buf = gc % Cfg::NBUF;
+        const uint32_t bph = (gc / Cfg::NBUF) & 1;
+        if (!mbar_wait(&acce_bar[buf], bph ^ 1u, ab, kTimeoutAccEmpty)) {
           aborted = true;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-        const uint32_t sb = sa + Cfg::NPARTS * Cfg::A_TILE;
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        const int kb_end = (num_kb - kb0 < Cfg::CHUNK_KB) ? num_kb : kb0 + Cfg::CHUNK_KB;
+        for (int kb = kb0; kb < kb_end; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::NPARTS * Cfg::A_TILE;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t acc_in = (kb | kk) != 0;
-          if (KIND == kF16) {
-            const uint64_t ad = p.a_mn ? sdesc_sw128(sa + kk * 2048, 64 * 128, 1024)
-                                       : sdesc_sw128(sa + kk * 32, 16, 1024);
-            const uint64_t bd = p.b_mn ? sdesc_sw128(sb + kk * 2048, 64 * 128, 1024)
-                                       : sdesc_sw128(sb + kk * 32, 16, 1024);
-            mma_f16(d_tmem, ad, bd, idesc_v, acc_in);
-          } else {
-            const uint64_t ah = sdesc_sw128(sa + kk * 32, 16, 1024);
-            const uint64_t al = sdesc_sw128(sa + Cfg::A_TILE + kk * 32, 16, 1024);
-            const uint64_t bh = sdesc_sw128(sb + kk * 32, 16, 1024);
-            const uint64_t bl = sdesc_sw128(sb + Cfg::B_TILE + kk * 32, 16, 1024);
-            mma_tf32(d_tmem, al, bh, idesc_v, acc_in);  // small terms first
-            mma_tf32(d_tmem, ah, bl, idesc_v, 1u);
-            mma_tf32(d_tmem, ah, bh, idesc_v, 1u);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc_in = (kb != kb0 || kk != 0) ? 1u : 0u;
+            if (KIND == kF16) {
+              const uint64_t ad = p.a_mn ? sdesc_sw128(sa + kk * 2048, 64 * 128, 1024)
+                                         : sdesc_sw128(sa + kk * 32, 16, 1024);
+              const uint64_t bd = p.b_mn ? sdesc_sw128(sb + kk * 2048, 64 * 128, 1024)
+                                         : sdesc_sw128(sb + kk * 32, 16, 1024);
+              mma_f16(d_tmem, ad, bd, idesc_v, acc_in);
+            } else {
+              const uint64_t ah = sdesc_sw128(sa + kk * 32, 16, 1024);
+              const uint64_t al = sdesc_sw128(sa + Cfg::A_TILE + kk * 32, 16, 1024);
+              const uint64_t bh = sdesc_sw128(sb + kk * 32, 16, 1024);
+              const uint64_t bl = sdesc_sw128(sb + Cfg::B_TILE + kk * 32, 16, 1024);
+              mma_tf32(d_tmem, al, bh, idesc_v, acc_in);  // small terms first
+              mma_tf32(d_tmem, ah, bl, idesc_v, 1u);
+              mma_tf32(d_tmem, ah, bh, idesc_v, 1u);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
-        tc_commit(&empty_bar[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (aborted) break;
+        tc_commit(&accf_bar[buf]);
       }
-      if (aborted) break;
-      tc_commit(&accf_bar[acc]);
     }
     // Every MMA this thread issued must finish before TMEM is released.
     tc_commit(drain_bar);
@@ -390,30 +403,69 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = 32 * q + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t accph = (it >> 1) & 1;
-      if (!mbar_wait(&accf_bar[acc], accph, ab, kTimeoutAccFull)) break;
-      tc_fence_after();
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+    int gc = 0;
+    bool aborted = false;
+    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x) {
       int bz, mb, nb;
       decode_tile(p, t, bz, mb, nb);
       const int r = mb * BM + row_in_tile;
       const int ncol = (p.mode == kModeSyrk) ? BM : BN;
       const int n0 = nb * ncol;
+      const int nlim = (p.mode == kModeSyrk) ? p.M : p.N;
       const bool diag = (p.mode == kModeSyrk) && (mb == nb);
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + acc * BN;
+      if (KIND == kF16) {
+        // whole K in one TMEM accumulator
+        const int buf = gc % Cfg::NBUF;
+        const uint32_t bph = (gc / Cfg::NBUF) & 1;
+        ++gc;
+        if (!mbar_wait(&accf_bar[buf], bph, ab, kTimeoutAccFull)) break;
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < ncol / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tbase + c * 32, v);
-        tmem_ld_wait();
-        if (n0 + c * 32 < ((p.mode == kModeSyrk) ? p.M : p.N))
-          epilogue_chunk(p, bz, r, n0 + c * 32, v, diag);
+        for (int c = 0; c < ncol / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + buf * BN + c * 32, v);
+          tmem_ld_wait();
+          if (n0 + c * 32 < nlim) {
+            float f[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = u2f(v[j]);
+            epilogue_chunk(p, bz, r, n0 + c * 32, f, diag);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce_bar[buf]);
+      } else {
+        // K chunks: partial sums added here with round-to-nearest
+        float sum[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+        for (int kb0 = 0; kb0 < num_kb; kb0 += Cfg::CHUNK_KB, ++gc) {
+          const int buf = gc % Cfg::NBUF;
+          const uint32_t bph = (gc / Cfg::NBUF) & 1;
+          if (!mbar_wait(&accf_bar[buf], bph, ab, kTimeoutAccFull)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(lane_base + buf * BN + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[c * 32 + j] += u2f(v[j]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce_bar[buf]);
+        }
+        if (aborted) break;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          if (n0 + c * 32 < nlim) epilogue_chunk(p, bz, r, n0 + c * 32, sum + c * 32, diag);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce_bar[acc]);
     }
   }
 

@@ -1,0 +1,158 @@
+// Ozaki split on the GPU: per-row power-of-two scaling and balanced 7-bit
+// integer digits, bit for bit the digits of the reference's host split
+// (trnblas/ozaki.py:123-219, `split` with per="row"; a per-column split of B
+// is the per-row split of op(B)^T).
+//
+// For a logical R x K operand X (element (r, k) at X[r * rs + k * ks]):
+//   e_r   = frexp exponent of max_k |X[r, k]| (0 for an all-zero row);
+//   shift = 6 - e_r; if any row's shift leaves [-1022, 1023], every row is
+//           scaled by two factors 2^floor(shift/2) * 2^(shift - floor(shift/2))
+//           (the reference makes this choice once per operand);
+//   R     = X * scale (exact);  digit_0 = rint(R);  R -= digit_0;
+//   digit_s = rint(128 R); R = 128 R - digit_s ...  (fp64, round half even)
+// Digits (|d| <= 64) are written as int8 planes (slices, R, ldd), K-major,
+// zero beyond K; exponents as int32. Float inputs are widened exactly.
+#pragma once
+
+#include "common.cuh"
+
+namespace tb {
+
+struct SplitScratch {
+  unsigned long long* maxbits;  // R words: max |x| as IEEE bits (monotone for x >= 0)
+  int* shift_range;             // [0] = max shift, [1] = min shift (for the 2-factor rule)
+};
+
+// Pass 1: per-row max |x| (32 x 32 tiles, coalesced for either layout).
+template <typename T>
+__global__ void ozk_rowmax_kernel(const T* __restrict__ X, long long rs, long long ks, int R,
+                                  int K, unsigned long long* __restrict__ maxbits) {
+  __shared__ double tile[32][33];
+  const int k0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  if (ks == 1) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      tile[i][tx] = (r < R && k < K) ? fabs(static_cast<double>(__ldg(X + r * rs + k))) : 0.0;
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      tile[tx][i] =
+          (r < R && k < K) ? fabs(static_cast<double>(__ldg(X + r * rs + k * ks))) : 0.0;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(tile[i][tx]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long ob = __shfl_xor_sync(0xffffffffu, b, o);
+      b = ob > b ? ob : b;
+    }
+    if (tx == 0 && r0 + i < R && b != 0) atomicMax(maxbits + r0 + i, b);
+  }
+}
+
+// frexp exponent of a non-negative finite double given by its bits.
+__device__ __forceinline__ int frexp_exp_bits(unsigned long long b) {
+  if (b == 0) return 0;
+  const int E = static_cast<int>(b >> 52);
+  if (E > 0) return E - 1022;
+  // subnormal: value = m * 2^-1074 with m = b < 2^52
+  return (64 - __clzll(static_cast<long long>(b))) - 1074;
+}
+
+static __global__ void ozk_init_kernel(unsigned long long* maxbits, int R, int* shift_range) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < R) maxbits[i] = 0ull;
+  if (i == 0) {
+    shift_range[0] = -2147483647;
+    shift_range[1] = 2147483647;
+  }
+}
+
+// Pass 2: exponents and the operand-wide shift range.
+static __global__ void ozk_exps_kernel(const unsigned long long* __restrict__ maxbits, int R,
+                                       int* __restrict__ exps, int* __restrict__ shift_range) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  const int e = frexp_exp_bits(maxbits[r]);
+  exps[r] = e;
+  const int shift = 6 - e;
+  atomicMax(shift_range + 0, shift);
+  atomicMin(shift_range + 1, shift);
+}
+
+// Pass 3: digits. 32 x 32 tiles through shared memory; each thread produces
+// all `slices` digits of one element.
+template <typename T>
+__global__ void ozk_digits_kernel(const T* __restrict__ X, long long rs, long long ks, int R,
+                                  int K, int ldd, long long plane, int slices,
+                                  const int* __restrict__ exps,
+                                  const int* __restrict__ shift_range,
+                                  int8_t* __restrict__ digits) {
+  __shared__ double tile[32][33];
+  const int k0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  if (ks == 1) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      tile[i][tx] = (r < R && k < K) ? static_cast<double>(__ldg(X + r * rs + k)) : 0.0;
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      tile[tx][i] = (r < R && k < K) ? static_cast<double>(__ldg(X + r * rs + k * ks)) : 0.0;
+    }
+  }
+  __syncthreads();
+  const bool two = shift_range[0] > 1023 || shift_range[1] < -1022;
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, k = k0 + tx;
+    if (r >= R || k >= ldd) continue;
+    const long long o = static_cast<long long>(r) * ldd + k;
+    if (k >= K) {
+      for (int s = 0; s < slices; ++s) digits[s * plane + o] = 0;
+      continue;
+    }
+    const int shift = 6 - exps[r];
+    double v = tile[i][tx];
+    if (!two) {
+      v = v * pow2d(shift);
+    } else {
+      const int h = (shift >= 0) ? shift / 2 : -((-shift + 1) / 2);
+      v = v * pow2d(h);
+      v = v * pow2d(shift - h);
+    }
+    for (int s = 0; s < slices; ++s) {
+      if (s) v = v * 128.0;
+      const double d = rint(v);
+      if (s + 1 < slices) v = v - d;
+      digits[s * plane + o] = static_cast<int8_t>(static_cast<int>(d));
+    }
+  }
+}
+
+// Run the passes on `stream`. scratch.maxbits (R words) and
+// scratch.shift_range (2 ints) are initialised here.
+template <typename T>
+inline cudaError_t launch_split(const T* X, long long rs, long long ks, int R, int K, int ldd,
+                                int slices, int8_t* digits, int* exps, SplitScratch scratch,
+                                cudaStream_t stream) {
+  if ((R + 31) / 32 > 65535 || (ldd + 31) / 32 > 2147483647 / 2) return cudaErrorInvalidConfiguration;
+  ozk_init_kernel<<<(R + 255) / 256 + 1, 256, 0, stream>>>(scratch.maxbits, R,
+                                                          scratch.shift_range);
+  dim3 blk(32, 8);
+  dim3 g1(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((R + 31) / 32));
+  if (K > 0) ozk_rowmax_kernel<T><<<g1, blk, 0, stream>>>(X, rs, ks, R, K, scratch.maxbits);
+  ozk_exps_kernel<<<(R + 255) / 256, 256, 0, stream>>>(scratch.maxbits, R, exps,
+                                                       scratch.shift_range);
+  dim3 g3(static_cast<unsigned>((ldd + 31) / 32), static_cast<unsigned>((R + 31) / 32));
+  ozk_digits_kernel<T><<<g3, blk, 0, stream>>>(X, rs, ks, R, K, ldd,
+                                               static_cast<long long>(R) * ldd, slices, exps,
+                                               scratch.shift_range, digits);
+  return cudaGetLastError();
+}
+
+}  // namespace tb

@@ -1,0 +1,447 @@
+// Fused DF-MP2 pair energy on the int8 tensor cores.
+//
+// E = sum over occupied pairs i <= j (weight 1 if i == j, else 2) of
+//     sum_{a,b} T_ab (2 T_ab - T_ba) / (e_i + e_j - e_a - e_b),  T = B_i B_j^T,
+// following the reference's symmetric pair walk (trnblas/nki/dispatch.py:
+// 2648-2677: e_ij = e_ji, so off-diagonal pairs count twice).
+//
+// Numerics. Tensor-core fp32 accumulation truncates, a bias that grows with
+// naux and would put E off by ~1e-5 relative; the 1e-9 target needs T free of
+// systematic error. So B is split per row (i, a) into KS balanced 7-bit int8
+// digit planes with a power-of-two exponent (the Ozaki split of
+// trnblas/ozaki.py:123-219), and
+//     T_ab = 2^(e_ia + e_jb - 12) * (S_0 + 2^-7 S_1 + 2^-14 S_2),
+//     S_d  = sum_{s+t=d} D_s[i,a,:] . D_t[j,b,:]
+// with every S_d exact in int32 TMEM accumulators. What remains is the
+// truncation of the digit expansion (~2^-21 of the row maximum, zero-mean)
+// and round-to-nearest fp32 arithmetic in the epilogue, both unbiased; each
+// thread accumulates its terms in fp64 and the partial sums are reduced in a
+// fixed order, so the result is deterministic.
+//
+// Work unit: pair (i, j), a 128-row block R of a and a 64-column block C of b
+// with C >= 2R (64-blocks 2R and 2R+1 lie inside R). Two accumulator sets:
+//   X = B_i[R] . B_j[C]^T  ->  X[a, b] = T_ab
+//   Y = B_j[R] . B_i[C]^T  ->  Y[a, b] = T_ba
+// so T_ab and T_ba sit in the same TMEM lane and column: the epilogue needs
+// no transpose. Per (a, b): if the 64-blocks of a and b differ, the unit
+// accounts for both ordered pairs, [X(2X-Y) + Y(2Y-X)] / D; if they are the
+// same block, X(2X-Y) / D once; a in block 2R+1 with b in block 2R is skipped
+// (unit (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
+#include <algorithm>
+#include <string>
+
+#include "ozaki_split.cuh"
+#include "runtime.hpp"
+
+namespace tb {
+
+struct PairParams {
+  int nocc, nvir, naux_p;  // naux_p: K columns of the digit planes (multiple of 32)
+  long long pair_begin;
+  long long num_units;     // pairs * units_per_pair
+  int units_per_pair;
+  int nR, nC;              // 128-blocks and 64-blocks of nvir
+  const int* exps;         // nocc * nvir
+  const float* eps_occ;
+  const float* eps_vir;
+  double* partials;        // gridDim.x
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+template <int KS>
+struct PairCfg {
+  static constexpr int BM = 128, BN = 64, BK = 32;
+  static constexpr int A_PLANE = BM * BK, B_PLANE = BN * BK;
+  static constexpr int XA = 0;
+  static constexpr int XB = XA + KS * A_PLANE;
+  static constexpr int YA = XB + KS * B_PLANE;
+  static constexpr int YB = YA + KS * A_PLANE;
+  static constexpr int STAGE_BYTES = YB + KS * B_PLANE;
+  static constexpr int TX_BYTES = STAGE_BYTES;
+  static constexpr int Y_COL = KS * BN;  // TMEM column of the Y accumulators
+  static_assert(2 * KS * BN <= 512, "X and Y diagonals must fit TMEM");
+};
+
+__device__ __forceinline__ void pair_of(long long p, int& i, int& j) {
+  long long jj = static_cast<long long>((sqrt(8.0 * static_cast<double>(p) + 1.0) - 1.0) * 0.5);
+  while (jj * (jj + 1) / 2 > p) --jj;
+  while ((jj + 1) * (jj + 2) / 2 <= p) ++jj;
+  j = static_cast<int>(jj);
+  i = static_cast<int>(p - jj * (jj + 1) / 2);
+}
+
+__device__ __forceinline__ void unit_of(const PairParams& p, long long u, int& i, int& j, int& R,
+                                        int& C) {
+  const long long pr = u / p.units_per_pair;
+  int loc = static_cast<int>(u - pr * p.units_per_pair);
+  pair_of(p.pair_begin + pr, i, j);
+  R = 0;
+  while (R < p.nR) {
+    const int cnt = p.nC - 2 * R;
+    if (loc < cnt) break;
+    loc -= cnt;
+    ++R;
+  }
+  C = 2 * R + loc;
+}
+
+__device__ __forceinline__ float pow2f(int n) {
+  n = n < -126 ? -126 : (n > 127 ? 127 : n);
+  return __int_as_float((n + 127) << 23);
+}
+
+template <int KS, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    pair_energy_kernel(const __grid_constant__ CUtensorMap map_rows128,
+                       const __grid_constant__ CUtensorMap map_rows64, const PairParams p) {
+  using Cfg = PairCfg<KS>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;
+  uint64_t* acce_bar = accf_bar + 1;
+  uint64_t* drain_bar = acce_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  double* red = reinterpret_cast<double*>(smem + STAGES * Cfg::STAGE_BYTES + 128);  // [4]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Abort ab{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(accf_bar, 1);
+    mbar_init(acce_bar, 4);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    for (int w = 0; w < 4; ++w) red[w] = 0.0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_rows128);
+    tma_prefetch_desc(&map_rows64);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = p.naux_p / Cfg::BK;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool aborted = false;
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      int i, j, R, C;
+      unit_of(p, u, i, j, R, C);
+      const int ri = i * p.nvir, rj = j * p.nvir;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
+          aborted = true;
+          break;
+        }
+        uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
+        const int kc = kb * Cfg::BK;
+        tma_load_3d(st + Cfg::XA, &map_rows128, &full_bar[stage], kc, ri + 128 * R, 0);
+        tma_load_3d(st + Cfg::XB, &map_rows64, &full_bar[stage], kc, rj + 64 * C, 0);
+        tma_load_3d(st + Cfg::YA, &map_rows128, &full_bar[stage], kc, rj + 128 * R, 0);
+        tma_load_3d(st + Cfg::YB, &map_rows64, &full_bar[stage], kc, ri + 64 * C, 0);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (aborted || ab.raised()) {
+      int s = stage;
+      uint32_t ph = phase;
+      for (int k = 0; k < STAGES; ++k) {
+        if (s == 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        } else {
+          --s;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], ph))
+          if (globaltimer_ns() - t0 > 50000000ull) break;
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool aborted = false;
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x, ++it) {
+      if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) break;
+      tc_fence_after();
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
+          const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, 128, (KS - s) * Cfg::BN);
+          // X: A-plane s of B_i[R] against B-planes 0 .. KS-1-s of B_j[C]
+          mma_i8(tmem_base + s * Cfg::BN,
+                 sdesc_kmajor(st + Cfg::XA + s * Cfg::A_PLANE, 256, kSwz32),
+                 sdesc_kmajor(st + Cfg::XB, 256, kSwz32), id, acc_in);
+          // Y: A-plane s of B_j[R] against B-planes of B_i[C]
+          mma_i8(tmem_base + Cfg::Y_COL + s * Cfg::BN,
+                 sdesc_kmajor(st + Cfg::YA + s * Cfg::A_PLANE, 256, kSwz32),
+                 sdesc_kmajor(st + Cfg::YB, 256, kSwz32), id, acc_in);
+        }
+        tc_commit(&empty_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (aborted) break;
+      tc_commit(accf_bar);
+    }
+    tc_commit(drain_bar);
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(drain_bar, 0)) {
+      if (globaltimer_ns() - t0 > 100000000ull) {
+        ab.raise(kTimeoutDrain);
+        break;
+      }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int aloc = 32 * q + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+    double acc = 0.0;  // this thread's fp64 partial sum
+    int it = 0;
+    for (long long u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
+      if (!mbar_wait(accf_bar, it & 1, ab, kTimeoutAccFull)) break;
+      tc_fence_after();
+      int i, j, R, C;
+      unit_of(p, u, i, j, R, C);
+      const int a = 128 * R + aloc;
+      // lane mode: 2 = both ordered pairs, 1 = (a, b) once, 0 = skip
+      int mode = 2;
+      if (C == 2 * R + 1) mode = (aloc < 64) ? 2 : 1;
+      if (C == 2 * R) mode = (aloc < 64) ? 1 : 0;
+      if (a >= p.nvir) mode = 0;
+      const float w = (i == j) ? 1.0f : 2.0f;
+      double usum = 0.0;
+      if (mode) {
+        const int eia = p.exps[i * p.nvir + a], eja = p.exps[j * p.nvir + a];
+        const float da = (p.eps_occ[i] + p.eps_occ[j]) - p.eps_vir[a];
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t xv[KS][32], yv[KS][32];
+#pragma unroll
+          for (int d = 0; d < KS; ++d) {
+            tmem_ld32(lane_base + d * Cfg::BN + 32 * c, xv[d]);
+            tmem_ld32(lane_base + Cfg::Y_COL + d * Cfg::BN + 32 * c, yv[d]);
+          }
+          tmem_ld_wait();
+          const int b0 = 64 * C + 32 * c;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int b = b0 + jj;
+            if (b >= p.nvir) continue;
+            float xs = static_cast<float>(static_cast<int>(xv[KS - 1][jj]));
+            float ys = static_cast<float>(static_cast<int>(yv[KS - 1][jj]));
+#pragma unroll
+            for (int d = KS - 2; d >= 0; --d) {
+              xs = fmaf(xs, 0.0078125f, static_cast<float>(static_cast<int>(xv[d][jj])));
+              ys = fmaf(ys, 0.0078125f, static_cast<float>(static_cast<int>(yv[d][jj])));
+            }
+            const float X = xs * pow2f(eia + p.exps[j * p.nvir + b] - 12);
+            const float Y = ys * pow2f(eja + p.exps[i * p.nvir + b] - 12);
+            const float den = da - p.eps_vir[b];
+            float f = X * (2.0f * X - Y);
+            if (mode == 2) f += Y * (2.0f * Y - X);
+            usum += static_cast<double>(f / den);
+          }
+        }
+      }
+      acc += static_cast<double>(w) * usum;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar);
+    }
+    // warp reduction (fixed tree) then per-CTA partial
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) red[warp - 2] = acc;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) p.partials[blockIdx.x] = ((red[0] + red[1]) + red[2]) + red[3];
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// Sum the per-CTA partials in index order (deterministic).
+__global__ void pair_energy_finish(const double* partials, int n, double* energy) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    double s = 0.0;
+    for (int k = 0; k < n; ++k) s += partials[k];
+    *energy = s;
+  }
+}
+
+namespace {
+
+constexpr int kPairSlices = 3;
+constexpr int kPairStages = 4;
+constexpr int kMaxGrid = 1024;
+
+struct PairLayout {
+  long long naux_p, R;
+  size_t off_exps, off_max, off_range, off_part, total;
+};
+
+PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
+  PairLayout L{};
+  L.naux_p = round_up(std::max<long long>(naux, 1), 32);
+  L.R = nocc * nvir;
+  const size_t dig = static_cast<size_t>(round_up(kPairSlices * L.R * L.naux_p, 256));
+  L.off_exps = dig;
+  L.off_max = L.off_exps + round_up(4 * L.R, 256);
+  L.off_range = L.off_max + round_up(8 * L.R, 256);
+  L.off_part = L.off_range + 256;
+  L.total = L.off_part + round_up(8 * kMaxGrid, 256);
+  return L;
+}
+
+int units_per_pair(long long nvir) {
+  const int nR = static_cast<int>(ceil_div(nvir, 128)), nC = static_cast<int>(ceil_div(nvir, 64));
+  int u = 0;
+  for (int R = 0; R < nR; ++R) u += std::max(0, nC - 2 * R);
+  return u;
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+size_t trnblas_pair_energy_workspace_size(int64_t nocc, int64_t nvir, int64_t naux,
+                                          int64_t pair_begin, int64_t pair_end) {
+  (void)pair_begin;
+  (void)pair_end;
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return 256;
+  return pair_layout(nocc, nvir, naux).total;
+}
+
+int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B,
+                        const float* eps_occ, const float* eps_vir, int64_t pair_begin,
+                        int64_t pair_end, double* energy, void* workspace,
+                        size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const long long npairs_total = nocc * (nocc + 1) / 2;
+  if (nocc < 0 || nvir < 0 || naux < 0 || pair_begin < 0 || pair_end < pair_begin ||
+      pair_end > npairs_total) {
+    set_error("trnblas_pair_energy: bad sizes or pair range");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (!energy) {
+    set_error("trnblas_pair_energy: NULL energy pointer");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (nocc * nvir > (1ll << 31) - 1 - 128) {
+    set_error("trnblas_pair_energy: nocc * nvir must stay below 2^31");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (naux > ((1ll << 31) - 1) / (kPairSlices * 4096ll)) {
+    set_error("trnblas_pair_energy: naux too large for exact int32 diagonal sums");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (pair_end == pair_begin || nvir == 0 || naux == 0) {
+    cudaError_t e = cudaMemsetAsync(energy, 0, sizeof(double), stream);
+    return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "cudaMemsetAsync(energy)");
+  }
+  if (!B || !eps_occ || !eps_vir) {
+    set_error("trnblas_pair_energy: NULL operand");
+    return TRNBLAS_ERR_ARG;
+  }
+  int* status = status_word();
+  if (!status) return TRNBLAS_ERR_CUDA;
+  const int upp = units_per_pair(nvir);
+  const long long num_units = (pair_end - pair_begin) * static_cast<long long>(upp);
+  const int grid = static_cast<int>(
+      std::min<long long>(std::min<long long>(num_units, num_sms()), kMaxGrid));
+  const PairLayout L = pair_layout(nocc, nvir, naux);
+  if (!workspace || workspace_bytes < L.total) {
+    set_error("trnblas_pair_energy needs " + std::to_string(L.total) + " workspace bytes");
+    return TRNBLAS_ERR_WORKSPACE;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int8_t* dig = reinterpret_cast<int8_t*>(ws);
+  int* exps = reinterpret_cast<int*>(ws + L.off_exps);
+  SplitScratch sc{reinterpret_cast<unsigned long long*>(ws + L.off_max),
+                  reinterpret_cast<int*>(ws + L.off_range)};
+  double* partials = reinterpret_cast<double*>(ws + L.off_part);
+  cudaError_t e = launch_split(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
+                               static_cast<int>(L.naux_p), kPairSlices, dig, exps, sc, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
+
+  CUtensorMap m128, m64;
+  const uint64_t dims[3] = {static_cast<uint64_t>(L.naux_p), static_cast<uint64_t>(L.R),
+                            static_cast<uint64_t>(kPairSlices)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(L.naux_p),
+                               static_cast<uint64_t>(L.R * L.naux_p)};
+  const uint32_t box128[3] = {32, 128, kPairSlices};
+  const uint32_t box64[3] = {32, 64, kPairSlices};
+  if (!encode_map(&m128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 3, dims, strides, box128,
+                  CU_TENSOR_MAP_SWIZZLE_32B) ||
+      !encode_map(&m64, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 3, dims, strides, box64,
+                  CU_TENSOR_MAP_SWIZZLE_32B))
+    return TRNBLAS_ERR_ALIGN;
+
+  PairParams p{};
+  p.nocc = static_cast<int>(nocc);
+  p.nvir = static_cast<int>(nvir);
+  p.naux_p = static_cast<int>(L.naux_p);
+  p.pair_begin = pair_begin;
+  p.num_units = num_units;
+  p.units_per_pair = upp;
+  p.nR = static_cast<int>(ceil_div(nvir, 128));
+  p.nC = static_cast<int>(ceil_div(nvir, 64));
+  p.exps = exps;
+  p.eps_occ = eps_occ;
+  p.eps_vir = eps_vir;
+  p.partials = partials;
+  p.status = status;
+  p.timeout_ns = wait_timeout_ns();
+
+  constexpr int smem = kPairStages * PairCfg<kPairSlices>::STAGE_BYTES + 1024 + 256;
+  auto kern = pair_energy_kernel<kPairSlices, kPairStages>;
+  static bool attr_set[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  kern<<<grid, 192, smem, stream>>>(m128, m64, p);
+  pair_energy_finish<<<1, 32, 0, stream>>>(partials, grid, energy);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "pair energy launch");
+}
+
+}  // extern "C"

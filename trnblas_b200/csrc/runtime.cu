@@ -136,6 +136,59 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
   return true;
 }
 
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, int rank,
+                const uint64_t* dims, const uint64_t* strides_elems, const uint32_t* box,
+                CUtensorMapSwizzle swizzle) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!load_encode()) return false;
+  }
+  if (rank < 1 || rank > 5) {
+    set_error("bad tensor map rank");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
+    set_error("operand base address is not 16-byte aligned");
+    return false;
+  }
+  const uint32_t span = swizzle == CU_TENSOR_MAP_SWIZZLE_128B ? 128
+                        : swizzle == CU_TENSOR_MAP_SWIZZLE_64B ? 64
+                        : swizzle == CU_TENSOR_MAP_SWIZZLE_32B ? 32 : 0;
+  if (span ? box[0] * static_cast<uint32_t>(esize) != span
+           : (box[0] * static_cast<uint32_t>(esize)) % 16 != 0) {
+    set_error("tensor map inner box does not match the swizzle span");
+    return false;
+  }
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] == 0 || box[i] == 0 || box[i] > 256) {
+      set_error("bad tensor map geometry");
+      return false;
+    }
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    const uint64_t b = strides_elems[i] * static_cast<uint64_t>(esize);
+    if ((b & 15) != 0 || b >= (1ull << 40)) {
+      set_error("tensor map stride is not a multiple of 16 bytes (or too large)");
+      return false;
+    }
+    st[i] = b;
+  }
+  CUresult r = g_encode(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st,
+                        bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
+    return false;
+  }
+  return true;
+}
+
 // One CTA waits on an mbarrier whose phase never completes, gives up after
 // `timeout_ns`, records kTimeoutTest and returns.
 __global__ void wait_selftest_kernel(int* status, unsigned long long timeout_ns) {

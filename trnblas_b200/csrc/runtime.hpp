@@ -36,6 +36,13 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
 inline long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
 inline long long round_up(long long a, long long b) { return ceil_div(a, b) * b; }
 
+// General tiled map: rank 1..5, given swizzle (CU_TENSOR_MAP_SWIZZLE_*);
+// box0 * esize must equal the swizzle span (or be a multiple of 16 bytes
+// without swizzle). Strides are in elements for dims 1..rank-1.
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, int rank,
+                const uint64_t* dims, const uint64_t* strides_elems, const uint32_t* box,
+                CUtensorMapSwizzle swizzle);
+
 // Kernel wait bound in ns (TRNBLAS_B200_WAIT_NS overrides; tests shorten it).
 unsigned long long wait_timeout_ns();
 

@@ -433,3 +433,91 @@ def syrk(
         if add:
             R = _symmetrize(R + beta * Cd)
     return R.to(home) if home != dev else R
+
+
+# ── fp64-class GEMM (Ozaki on the int8 tensor cores) ─────────────────────────
+
+MIN_SLICES, MAX_SLICES, DEFAULT_SLICES = 1, 12, 8
+
+
+def check_slices(slices) -> int:
+    """`slices` as an int in [1, 12]: TypeError for a non-int (or bool),
+    ValueError out of range (trnblas/ozaki.py:51-58)."""
+    import numpy as np
+
+    if isinstance(slices, bool) or not isinstance(slices, (int, np.integer)):
+        raise TypeError(f"slices must be an int, got {type(slices).__name__}")
+    k = int(slices)
+    if not MIN_SLICES <= k <= MAX_SLICES:
+        raise ValueError(f"slices must be in [{MIN_SLICES}, {MAX_SLICES}], got {k}")
+    return k
+
+
+def _gemm_fp64_device(a: torch.Tensor, b: torch.Tensor, k: int) -> torch.Tensor:
+    """fp64 a @ b on the Ozaki int8 kernel (a, b finite fp64 on one CUDA device)."""
+    M, K = a.shape
+    Nn = b.shape[1]
+    dev = a.device
+    out = torch.empty((M, Nn), dtype=torch.float64, device=dev)
+    if M == 0 or Nn == 0:
+        return out
+    at, lda, ta = _f32_operand(a)  # any unit-stride layout; the split kernels read strides
+    bt, ldb, tb = _f32_operand(b)
+    ws_bytes = N.lib().trnblas_gemm_fp64_workspace_size(M, Nn, K, k)
+    ws = N.workspace(ws_bytes, dev)
+    rc = N.lib().trnblas_gemm_fp64(
+        M, Nn, K, N.ptr(at), lda, int(ta), N.ptr(bt), ldb, int(tb), k,
+        N.ptr(out), Nn, N.ptr(ws), ws_bytes, N.stream_ptr(dev),
+    )
+    N.check(rc, "trnblas_gemm_fp64")
+    return out
+
+
+def gemm_fp64(
+    A: torch.Tensor,
+    B: torch.Tensor,
+    *,
+    slices: int = DEFAULT_SLICES,
+    transA: bool = False,
+    transB: bool = False,
+) -> torch.Tensor:
+    """fp64-class op(A) @ op(B) by Ozaki splitting on the int8 tensor cores.
+
+    A is split per row and B per column into `slices` (k) balanced 7-bit
+    integer digits with one power-of-two exponent per row / column (the
+    reference's split, trnblas/ozaki.py:123-219, bit for bit). Each diagonal
+    s + t = d <= k - 1 of slice products is summed exactly in int32 on the
+    tensor cores, and the diagonals are recombined in fp64 (smallest first)
+    with the exponents. k (k + 1) / 2 slice products; k = 8 (default) gives
+    host fp64 BLAS accuracy on well-scaled data, wide dynamic ranges within a
+    row / column need more slices. 1 <= slices <= 12.
+
+    A (M, K) and B (K, N) are 2-D real tensors of any float dtype (computed as
+    fp64); returns float64 (M, N) on A's device. Non-finite operands (which the
+    digits cannot represent) are multiplied by torch.matmul in fp64, as the
+    reference does (trnblas/nki/dispatch.py:958-980).
+    """
+    k = check_slices(slices)
+    transA, transB = trans_flag(transA, "transA"), trans_flag(transB, "transB")
+    for name, X in (("A", A), ("B", B)):
+        if not isinstance(X, torch.Tensor) or X.dim() != 2:
+            raise ValueError(f"gemm_fp64: {name} must be a 2-D tensor")
+        if not X.is_floating_point():
+            raise TypeError(f"gemm_fp64: {name} must be a real floating tensor, got {X.dtype}")
+    a = A.mT if transA else A
+    b = B.mT if transB else B
+    if a.shape[1] != b.shape[0]:
+        raise ValueError(
+            f"gemm_fp64: inner dimensions differ: op(A) {tuple(a.shape)}, op(B) {tuple(b.shape)}"
+        )
+    home = A.device
+    dev = _cuda_device(A, B)
+    a = _to(a.detach(), dev).to(torch.float64)
+    b = _to(b.detach(), dev).to(torch.float64)
+    if a.shape[1] == 0:
+        r = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float64, device=dev)
+    elif not (bool(torch.isfinite(a).all()) and bool(torch.isfinite(b).all())):
+        r = torch.matmul(a, b)
+    else:
+        r = _gemm_fp64_device(a, b, k)
+    return r.to(home) if home != dev else r

@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(192, 1)
         const int buf = gc % Cfg::NBUF;
         const uint32_t bph = (gc / Cfg::NBUF) & 1;
         ++gc;
-        if (!mbar_wait(&accf_bar[buf], bph, ab, kTimeoutAccFull)) break;
+        if (!mbar_wait_warp(&accf_bar[buf], bph, ab, kTimeoutAccFull)) break;
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < ncol / 32; ++c) {
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb0 = 0; kb0 < num_kb; kb0 += Cfg::CHUNK_KB, ++gc) {
           const int buf = gc % Cfg::NBUF;
           const uint32_t bph = (gc / Cfg::NBUF) & 1;
-          if (!mbar_wait(&accf_bar[buf], bph, ab, kTimeoutAccFull)) {
+          if (!mbar_wait_warp(&accf_bar[buf], bph, ab, kTimeoutAccFull)) {
             aborted = true;
             break;
           }
@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();  // lane 0 arrives from the MMA role, 1..31 straight here
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }

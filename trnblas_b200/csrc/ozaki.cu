@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(192, 1)
     const int off = -12 - 7 * (ks - 1);
     int it = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-      if (!mbar_wait(accf_bar, it & 1, ab, kTimeoutAccFull)) break;
+      if (!mbar_wait_warp(accf_bar, it & 1, ab, kTimeoutAccFull)) break;
       tc_fence_after();
       const int mb = t % p.tiles_m, nb = t / p.tiles_m;
       const int r = mb * BM + 32 * q + lane;
@@ -223,6 +223,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();  // lane 0 arrives from the MMA role, 1..31 straight here
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }

@@ -7,26 +7,31 @@
 //
 // Numerics. Tensor-core fp32 accumulation truncates, a bias that grows with
 // naux and would put E off by ~1e-5 relative; the 1e-9 target needs T free of
-// systematic error. So B is split per row (i, a) into KS balanced 7-bit int8
-// digit planes with a power-of-two exponent (the Ozaki split of
+// systematic error. So B is split per row (i, a) into KS = 5 balanced 7-bit
+// int8 digit planes with a power-of-two exponent (the Ozaki split of
 // trnblas/ozaki.py:123-219), and
-//     T_ab = 2^(e_ia + e_jb - 12) * (S_0 + 2^-7 S_1 + 2^-14 S_2),
+//     T_ab = 2^(e_ia + e_jb - 12) * sum_{d <= 4} 2^(-7 d) S_d,
 //     S_d  = sum_{s+t=d} D_s[i,a,:] . D_t[j,b,:]
-// with every S_d exact in int32 TMEM accumulators. What remains is the
-// truncation of the digit expansion (~2^-21 of the row maximum, zero-mean)
-// and round-to-nearest fp32 arithmetic in the epilogue, both unbiased; each
-// thread accumulates its terms in fp64 and the partial sums are reduced in a
-// fixed order, so the result is deterministic.
+// with every S_d exact in int32 TMEM accumulators. Fewer digits leave a
+// measurable bias in E (3 slices: ~7e-8 relative at nocc/nvir/naux =
+// 48/432/1152, 4 slices with diagonals <= 3: ~2e-9); 5 slices with diagonals
+// <= 4 are at ~1e-12. The epilogue folds the diagonals in fp32 with
+// round-to-nearest, forms the terms in fp32 and accumulates them per thread
+// in fp64; partial sums are reduced in a fixed order, so the result is
+// deterministic.
 //
 // Work unit: pair (i, j), a 128-row block R of a and a 64-column block C of b
-// with C >= 2R (64-blocks 2R and 2R+1 lie inside R). Two accumulator sets:
+// with C >= 2R (64-blocks 2R and 2R+1 lie inside R). Two passes over naux
+// into the same TMEM accumulators (5 diagonals x 64 columns):
 //   X = B_i[R] . B_j[C]^T  ->  X[a, b] = T_ab
 //   Y = B_j[R] . B_i[C]^T  ->  Y[a, b] = T_ba
-// so T_ab and T_ba sit in the same TMEM lane and column: the epilogue needs
-// no transpose. Per (a, b): if the 64-blocks of a and b differ, the unit
-// accounts for both ordered pairs, [X(2X-Y) + Y(2Y-X)] / D; if they are the
-// same block, X(2X-Y) / D once; a in block 2R+1 with b in block 2R is skipped
-// (unit (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
+// so T_ab and T_ba land in the same TMEM lane and column: no transpose. The
+// epilogue folds X into 64 registers per thread and releases TMEM before the
+// Y pass, then Y, then computes the terms from registers while the next
+// unit's X pass runs. Per (a, b): if the 64-blocks of a and b differ, the
+// unit accounts for both ordered pairs, [X(2X-Y) + Y(2Y-X)] / D; if they are
+// the same block, X(2X-Y) / D once; a in block 2R+1 with b in block 2R is
+// skipped (unit (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
 #include <algorithm>
 #include <string>
 
@@ -53,14 +58,10 @@ template <int KS>
 struct PairCfg {
   static constexpr int BM = 128, BN = 64, BK = 32;
   static constexpr int A_PLANE = BM * BK, B_PLANE = BN * BK;
-  static constexpr int XA = 0;
-  static constexpr int XB = XA + KS * A_PLANE;
-  static constexpr int YA = XB + KS * B_PLANE;
-  static constexpr int YB = YA + KS * A_PLANE;
-  static constexpr int STAGE_BYTES = YB + KS * B_PLANE;
-  static constexpr int TX_BYTES = STAGE_BYTES;
-  static constexpr int Y_COL = KS * BN;  // TMEM column of the Y accumulators
-  static_assert(2 * KS * BN <= 512, "X and Y diagonals must fit TMEM");
+  static constexpr int A_OFF = 0;
+  static constexpr int B_OFF = KS * A_PLANE;
+  static constexpr int STAGE_BYTES = KS * (A_PLANE + B_PLANE);
+  static_assert(KS * BN <= 512, "the diagonals of one pass must fit TMEM");
 };
 
 __device__ __forceinline__ void pair_of(long long p, int& i, int& j) {
@@ -141,21 +142,23 @@ __global__ void __launch_bounds__(192, 1)
       int i, j, R, C;
       unit_of(p, u, i, j, R, C);
       const int ri = i * p.nvir, rj = j * p.nvir;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
-          aborted = true;
-          break;
-        }
-        uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
-        const int kc = kb * Cfg::BK;
-        tma_load_3d(st + Cfg::XA, &map_rows128, &full_bar[stage], kc, ri + 128 * R, 0);
-        tma_load_3d(st + Cfg::XB, &map_rows64, &full_bar[stage], kc, rj + 64 * C, 0);
-        tma_load_3d(st + Cfg::YA, &map_rows128, &full_bar[stage], kc, rj + 128 * R, 0);
-        tma_load_3d(st + Cfg::YB, &map_rows64, &full_bar[stage], kc, ri + 64 * C, 0);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+      for (int pass = 0; pass < 2 && !aborted; ++pass) {
+        const int ra = (pass == 0 ? ri : rj) + 128 * R;  // A rows: B_i[R] then B_j[R]
+        const int rb = (pass == 0 ? rj : ri) + 64 * C;   // B rows: B_j[C] then B_i[C]
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
+            aborted = true;
+            break;
+          }
+          uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          const int kc = kb * Cfg::BK;
+          tma_load_3d(st + Cfg::A_OFF, &map_rows128, &full_bar[stage], kc, ra, 0);
+          tma_load_3d(st + Cfg::B_OFF, &map_rows64, &full_bar[stage], kc, rb, 0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
     }
@@ -178,39 +181,43 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ MMA issuer
     int stage = 0;
     uint32_t phase = 0;
-    int it = 0;
+    int it = 0;  // passes issued
     bool aborted = false;
-    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x, ++it) {
-      if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) break;
-      tc_fence_after();
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      for (int pass = 0; pass < 2 && !aborted; ++pass, ++it) {
+        if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) {
           aborted = true;
           break;
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
 #pragma unroll
-        for (int s = 0; s < KS; ++s) {
-          const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
-          const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, 128, (KS - s) * Cfg::BN);
-          // X: A-plane s of B_i[R] against B-planes 0 .. KS-1-s of B_j[C]
-          mma_i8(tmem_base + s * Cfg::BN,
-                 sdesc_kmajor(st + Cfg::XA + s * Cfg::A_PLANE, 256, kSwz32),
-                 sdesc_kmajor(st + Cfg::XB, 256, kSwz32), id, acc_in);
-          // Y: A-plane s of B_j[R] against B-planes of B_i[C]
-          mma_i8(tmem_base + Cfg::Y_COL + s * Cfg::BN,
-                 sdesc_kmajor(st + Cfg::YA + s * Cfg::A_PLANE, 256, kSwz32),
-                 sdesc_kmajor(st + Cfg::YB, 256, kSwz32), id, acc_in);
+          for (int s = 0; s < KS; ++s) {
+            const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
+            const uint64_t ad = sdesc_kmajor(st + Cfg::A_OFF + s * Cfg::A_PLANE, 256, kSwz32);
+#pragma unroll
+            for (int t0 = 0; t0 < KS - s; t0 += 4) {
+              const int np = (KS - s - t0 < 4) ? KS - s - t0 : 4;
+              const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, 128, np * Cfg::BN);
+              mma_i8(tmem_base + (s + t0) * Cfg::BN, ad,
+                     sdesc_kmajor(st + Cfg::B_OFF + t0 * Cfg::B_PLANE, 256, kSwz32), id, acc_in);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        tc_commit(&empty_bar[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (aborted) break;
+        tc_commit(accf_bar);
       }
-      if (aborted) break;
-      tc_commit(accf_bar);
     }
     tc_commit(drain_bar);
     const unsigned long long t0 = globaltimer_ns();
@@ -227,9 +234,40 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
     double acc = 0.0;  // this thread's fp64 partial sum
     int it = 0;
-    for (long long u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
-      if (!mbar_wait(accf_bar, it & 1, ab, kTimeoutAccFull)) break;
-      tc_fence_after();
+    bool aborted = false;
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      // fold the KS diagonals of one pass into 64 fp32 values (unscaled T)
+      float xt[64], yt[64];
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass, ++it) {
+        if (!mbar_wait_warp(accf_bar, it & 1, ab, kTimeoutAccFull)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[KS][16];
+#pragma unroll
+          for (int d = 0; d < KS; ++d) tmem_ld16(lane_base + d * Cfg::BN + 16 * c, v[d]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            float t = static_cast<float>(static_cast<int>(v[KS - 1][jj]));
+#pragma unroll
+            for (int d = KS - 2; d >= 0; --d)
+              t = fmaf(t, 0.0078125f, static_cast<float>(static_cast<int>(v[d][jj])));
+            if (pass == 0)
+              xt[16 * c + jj] = t;
+            else
+              yt[16 * c + jj] = t;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar);  // TMEM free for the next pass
+      }
+      if (aborted) break;
       int i, j, R, C;
       unit_of(p, u, i, j, R, C);
       const int a = 128 * R + aloc;
@@ -238,34 +276,17 @@ __global__ void __launch_bounds__(192, 1)
       if (C == 2 * R + 1) mode = (aloc < 64) ? 2 : 1;
       if (C == 2 * R) mode = (aloc < 64) ? 1 : 0;
       if (a >= p.nvir) mode = 0;
-      const float w = (i == j) ? 1.0f : 2.0f;
       double usum = 0.0;
       if (mode) {
         const int eia = p.exps[i * p.nvir + a], eja = p.exps[j * p.nvir + a];
         const float da = (p.eps_occ[i] + p.eps_occ[j]) - p.eps_vir[a];
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t xv[KS][32], yv[KS][32];
+        const int b0 = 64 * C;
 #pragma unroll
-          for (int d = 0; d < KS; ++d) {
-            tmem_ld32(lane_base + d * Cfg::BN + 32 * c, xv[d]);
-            tmem_ld32(lane_base + Cfg::Y_COL + d * Cfg::BN + 32 * c, yv[d]);
-          }
-          tmem_ld_wait();
-          const int b0 = 64 * C + 32 * c;
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int b = b0 + jj;
-            if (b >= p.nvir) continue;
-            float xs = static_cast<float>(static_cast<int>(xv[KS - 1][jj]));
-            float ys = static_cast<float>(static_cast<int>(yv[KS - 1][jj]));
-#pragma unroll
-            for (int d = KS - 2; d >= 0; --d) {
-              xs = fmaf(xs, 0.0078125f, static_cast<float>(static_cast<int>(xv[d][jj])));
-              ys = fmaf(ys, 0.0078125f, static_cast<float>(static_cast<int>(yv[d][jj])));
-            }
-            const float X = xs * pow2f(eia + p.exps[j * p.nvir + b] - 12);
-            const float Y = ys * pow2f(eja + p.exps[i * p.nvir + b] - 12);
+        for (int jj = 0; jj < 64; ++jj) {
+          const int b = b0 + jj;
+          if (b < p.nvir) {
+            const float X = xt[jj] * pow2f(eia + p.exps[j * p.nvir + b] - 12);
+            const float Y = yt[jj] * pow2f(eja + p.exps[i * p.nvir + b] - 12);
             const float den = da - p.eps_vir[b];
             float f = X * (2.0f * X - Y);
             if (mode == 2) f += Y * (2.0f * Y - X);
@@ -273,10 +294,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      acc += static_cast<double>(w) * usum;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce_bar);
+      acc += ((i == j) ? 1.0 : 2.0) * usum;
     }
     // warp reduction (fixed tree) then per-CTA partial
 #pragma unroll
@@ -288,6 +306,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (threadIdx.x == 0) p.partials[blockIdx.x] = ((red[0] + red[1]) + red[2]) + red[3];
   if (warp == 1) {
+    __syncwarp();  // lane 0 arrives from the MMA role, 1..31 straight here
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
@@ -304,8 +323,8 @@ __global__ void pair_energy_finish(const double* partials, int n, double* energy
 
 namespace {
 
-constexpr int kPairSlices = 3;
-constexpr int kPairStages = 4;
+constexpr int kPairSlices = 5;
+constexpr int kPairStages = 6;
 constexpr int kMaxGrid = 1024;
 
 struct PairLayout {

@@ -16,9 +16,11 @@
 // measurable bias in E (3 slices: ~7e-8 relative at nocc/nvir/naux =
 // 48/432/1152, 4 slices with diagonals <= 3: ~2e-9); 5 slices with diagonals
 // <= 4 are at ~1e-12. The epilogue folds the diagonals in fp32 with
-// round-to-nearest, forms the terms in fp32 and accumulates them per thread
-// in fp64; partial sums are reduced in a fixed order, so the result is
-// deterministic.
+// round-to-nearest and forms each numerator T_ab (2 T_ab - T_ba) in fp32
+// (independent rounding per term, which averages out); the denominators
+// e_i + e_j - e_a - e_b are exact in fp64 and the quotient is taken and
+// accumulated per thread in fp64. Partial sums are reduced in a fixed
+// order, so the result is deterministic.
 //
 // Work unit: pair (i, j), a 128-row block R of a and a 64-column block C of b
 // with C >= 2R (64-blocks 2R and 2R+1 lie inside R). Two passes over naux
@@ -279,7 +281,11 @@ __global__ void __launch_bounds__(192, 1)
       double usum = 0.0;
       if (mode) {
         const int eia = p.exps[i * p.nvir + a], eja = p.exps[j * p.nvir + a];
-        const float da = (p.eps_occ[i] + p.eps_occ[j]) - p.eps_vir[a];
+        // Denominators in fp64, where these sums and differences of fp32
+        // values are exact: an fp32 e_i + e_j would carry one rounding error
+        // shared by every term of the pair, which does not average out.
+        const double da = (static_cast<double>(p.eps_occ[i]) + static_cast<double>(p.eps_occ[j])) -
+                          static_cast<double>(p.eps_vir[a]);
         const int b0 = 64 * C;
 #pragma unroll
         for (int jj = 0; jj < 64; ++jj) {
@@ -287,10 +293,10 @@ __global__ void __launch_bounds__(192, 1)
           if (b < p.nvir) {
             const float X = xt[jj] * pow2f(eia + p.exps[j * p.nvir + b] - 12);
             const float Y = yt[jj] * pow2f(eja + p.exps[i * p.nvir + b] - 12);
-            const float den = da - p.eps_vir[b];
+            const double den = da - static_cast<double>(p.eps_vir[b]);
             float f = X * (2.0f * X - Y);
             if (mode == 2) f += Y * (2.0f * Y - X);
-            usum += static_cast<double>(f / den);
+            usum += static_cast<double>(f) / den;
           }
         }
       }

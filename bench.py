@@ -1,0 +1,557 @@
+"""Benchmark of the trnblas_b200 hot path (one JSON line on rank 0).
+
+Default workload (the metric's "1/2/4/8 B200" setting):
+the 2-D output-block sharded GEMM C = A @ B, M = N = K = 32768, bf16
+(`trnblas_b200.parallel.gemm_2d`), one step = the whole GEMM over all ranks;
+value = whole-job TFLOP/s. The same line carries the DF-MP2 pair-energy step
+of config 5 (nocc 96, nvir 2208, naux 6912, pairs sharded over ranks) in ms.
+Other workloads (--workload): gemm_fp32 (config 5a fp32), gemm8192_bf16 /
+gemm8192_fp32 (single-GPU 8192^3), batched (config 2a), syrk (config 2b),
+gemm_fp64 (config 4), pair3 (config 3), pair5 (config 5b alone).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+
+Inputs are seeded synthetic tensors with the BASELINE shapes and
+distributions, generated on the device (inputs far larger than L2, so no L2
+flush is needed between steps). Timing: CUDA events on the launching stream,
+barrier + synchronize around the K timed steps, max over ranks.
+
+`--impl reference` times the reference's CPU path (its torch/CPU route,
+restated in `oracle/`) on the host cores, rank 0 only, on a bounded sample of
+the same workload; the other ranks exit without work.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+REASON_BITS = {
+    0x1: "gpu_idle",
+    0x2: "applications_clocks_setting",
+    0x4: "sw_power_cap",
+    0x8: "hw_slowdown",
+    0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+def peaks():
+    if PEAKS_FILE.exists():
+        d = json.loads(PEAKS_FILE.read_text())
+        return d, "measured"
+    return FALLBACK, "fallback"
+
+
+# ── distributed plumbing ─────────────────────────────────────────────────────
+
+
+def setup_dist(n):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}; launch with torchrun --nproc-per-node {n}")
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group(
+            "nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+            device_id=torch.device("cuda", local),
+        )
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ── clocks during the timed region ───────────────────────────────────────────
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's SM clock and throttle reasons."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,power.draw",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 3:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+                bits = int(parts[2], 16)
+            except ValueError:
+                continue
+            for b, name in REASON_BITS.items():
+                if bits & b:
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx,
+            "reasons": sorted(reasons - {"gpu_idle"}),
+            "samples": len(sm),
+        }
+
+
+# ── timing helpers ───────────────────────────────────────────────────────────
+
+
+def timed_steps(step, steps, warmup, world, gpu):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(gpu) as cs:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    return max_over_ranks(ms, world), cs.summary()
+
+
+def kernel_avg_ms(events):
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in events) / max(len(events), 1)
+
+
+def read_traffic(name: str):
+    """Per-launch DRAM bytes for a kernel/workload from its ncu summary in
+    profiles/ (a line 'traffic_bytes_per_launch: <int>'), or None."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(ln.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+# ── CPU baseline (the reference's CPU route, restated) ──────────────────────
+
+
+def cpu_gemm_sample(n: int, dtype: torch.dtype, budget_s: float = 12.0):
+    """TFLOP/s of torch CPU matmul (the reference's host route for gemm) on a
+    row sample of an n x n x n product, sized to ~budget_s seconds."""
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(5)
+    B = (2 * torch.rand(n, n, generator=g) - 1).to(dtype)
+    rows = 64
+    A = (2 * torch.rand(rows, n, generator=g) - 1).to(dtype)
+    t0 = time.perf_counter()
+    torch.matmul(A, B)
+    t1 = time.perf_counter()
+    per_row = max((t1 - t0) / rows, 1e-6)
+    rows = int(max(64, min(n, budget_s / 2 / per_row)))
+    A = (2 * torch.rand(rows, n, generator=g) - 1).to(dtype)
+    torch.matmul(A[:64], B)  # warm
+    t0 = time.perf_counter()
+    torch.matmul(A, B)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * n * n / dt / 1e12, threads, f"{rows} x {n} rows of the {n}^3 product, {dtype}"
+
+
+def cpu_pair_sample(nocc, nvir, naux, budget_s: float = 12.0):
+    """Energy-step ms of the reference's chunked CPU energy (oracle restatement,
+    fp32 torch on the host), extrapolated from a pair-count sample."""
+    from oracle import pair_energy as PE
+
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(6)
+    npairs = PE.n_pairs(nocc)
+    # sample: rows i (all j) of the reference's aten_rows route, on a subset of B
+    B = (0.05 * torch.randn(nocc, nvir, naux, generator=g))
+    eo = torch.sort(-20 + 19.7 * torch.rand(nocc, generator=g)).values
+    ev = torch.sort(0.1 + 4.9 * torch.rand(nvir, generator=g)).values
+    Bf = B.reshape(nocc * nvir, naux)
+    t0 = time.perf_counter()
+    done = 0
+    i = 0
+    while time.perf_counter() - t0 < budget_s and i < nocc:
+        T = (Bf[i * nvir:(i + 1) * nvir] @ Bf.T).reshape(nvir, nocc, nvir).permute(1, 0, 2)
+        den = (eo[i] + eo).reshape(nocc, 1, 1) - ev.reshape(1, nvir, 1) - ev.reshape(1, 1, nvir)
+        float((T * (2 * T - T.transpose(-2, -1)) / den).sum())
+        done += nocc  # ordered pairs (i, j) for all j
+        i += 1
+    dt = time.perf_counter() - t0
+    full_ms = dt / done * (nocc * nocc) * 1e3
+    return full_ms, threads, f"{i} occupied rows ({done} ordered pairs of {nocc * nocc}) of the chunked fp32 energy, extrapolated by pair count"
+
+
+# ── workloads ────────────────────────────────────────────────────────────────
+
+
+def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
+    from trnblas_b200 import _native as N
+    from trnblas_b200 import parallel as tp
+
+    grid = tp.Grid2D() if world > 1 else _SingleGrid()
+    w = world
+    mw, nw = n // w, n // w
+    g = torch.Generator(device="cuda").manual_seed(5 + 1000 * rank)
+    A_sh = (2 * torch.rand(mw, n, device="cuda", generator=g) - 1).to(dtype)
+    B_sh = (2 * torch.rand(n, nw, device="cuda", generator=g) - 1).to(dtype)
+    k_chunks = 1 if world == 1 else 4
+    events = []
+
+    def step():
+        tp.gemm_2d(A_sh, B_sh, grid, k_chunks=k_chunks, kernel_events=events)
+
+    N.launch_count = 0
+    ms, clocks = timed_steps(step, args.steps, args.warmup, world, gpu)
+    launches_timed = N.launch_count  # includes warmup; normalised below
+    per_step_launches = launches_timed // (args.steps + args.warmup)
+    kern_ms = kernel_avg_ms(events[args.warmup * k_chunks:])
+    flops = 2.0 * n ** 3
+    value = flops / (ms / 1e3) / 1e12
+    # dominant kernel: one local GEMM launch (M/pr x N/pc x K/k_chunks)
+    pr, pc = grid.pr, grid.pc
+    launch_flops = 2.0 * (n // pr) * (n // pc) * (n // k_chunks)
+    achieved = launch_flops / (kern_ms / 1e3) / 1e12
+    pk, src = peaks()
+    peak = pk["bf16_tflops_sustained"] if dtype == torch.bfloat16 else pk["bf16_tflops_sustained"] / 6.0
+    # e2e: host operands (pinned), H2D + 2-D GEMM + D2H of this rank's C block
+    Ah = torch.empty(A_sh.shape, dtype=dtype, pin_memory=True).copy_(A_sh)
+    Bh = torch.empty(B_sh.shape, dtype=dtype, pin_memory=True).copy_(B_sh)
+    Ch = torch.empty((n // pr, n // pc), dtype=dtype, pin_memory=True)
+
+    def e2e_step():
+        a = Ah.to("cuda", non_blocking=True)
+        b = Bh.to("cuda", non_blocking=True)
+        c = tp.gemm_2d(a, b, grid, k_chunks=k_chunks)
+        Ch.copy_(c, non_blocking=True)
+
+    e2e_ms, _ = timed_steps(e2e_step, max(2, args.steps // 2), 1, world, gpu)
+    del Ah, Bh
+    es = A_sh.element_size()
+    line = {
+        "metric": f"GEMM TFLOP/s (2-D sharded, M=N=K={n}, {str(dtype).split('.')[-1]})",
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16" if dtype == torch.bfloat16 else "f32 (3xTF32 on tensor cores)",
+        "data": "synthetic (seeded uniform[-1,1] on device, BASELINE config 5 shapes)",
+        "config": {
+            "workload": f"config5a spmd gemm {n}^3",
+            "M": n, "N": n, "K": n, "grid": f"{pr}x{pc}", "k_chunks": k_chunks,
+            "parallelism": f"2d-output-block {pr}x{pc}",
+            "l2": "inputs larger than L2 (no flush needed)",
+        },
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "peak_source": f"{src} {'bf16 sustained' if dtype == torch.bfloat16 else 'bf16 sustained / 6 (3 tf32 products at half the bf16 rate)'}",
+            "kernel": "gemm_sm100_kernel",
+            "kernel_ms": round(kern_ms, 4),
+            "traffic": read_traffic("gemm_bf16_8192" if dtype == torch.bfloat16 else "gemm_fp32_8192"),
+            "traffic_note": "per launch of the 8192^3 ncu capture (profiles/), not scaled",
+        },
+        "e2e": {
+            "value": round(flops / (e2e_ms / 1e3) / 1e12, 2),
+            "unit": "TFLOP/s",
+            "ms_per_step": round(e2e_ms, 3),
+            "h2d_bytes_per_step": int((A_sh.numel() + B_sh.numel()) * es * world),
+            "d2h_bytes_per_step": int((n // pr) * (n // pc) * es * world),
+            "path": "trnblas_b200.parallel.gemm_2d on pinned host operands (all ranks)",
+        },
+        "clocks": clocks,
+        "gpu_launches": per_step_launches * args.steps,
+    }
+    del A_sh, B_sh
+    torch.cuda.empty_cache()
+    return line
+
+
+class _SingleGrid:
+    """A 1x1 grid without process groups (N = 1)."""
+
+    pr = pc = 1
+    r = c = rank = 0
+    world = 1
+    row_group = col_group = None
+
+    def block_rows(self, M):
+        return 0, M
+
+    def block_cols(self, N):
+        return 0, N
+
+
+def run_pair(args, rank, world, gpu, nocc, nvir, naux, steps=None, warmup=None):
+    from trnblas_b200 import _native as N
+    from trnblas_b200 import energy
+    from trnblas_b200 import parallel as tp
+
+    g = torch.Generator(device="cuda").manual_seed(6)  # same B on every rank
+    B = (0.05 * torch.randn(nocc, nvir, naux, device="cuda", generator=g))
+    eo = torch.sort(-20 + 19.7 * torch.rand(nocc, device="cuda", generator=g)).values
+    ev = torch.sort(0.1 + 4.9 * torch.rand(nvir, device="cuda", generator=g)).values
+    steps = steps or args.steps
+    warmup = warmup if warmup is not None else args.warmup
+    p0, p1 = energy.pair_ranges(nocc, world)[rank]
+    out = {}
+
+    def step():
+        e = energy.pair_range_energy(B, eo, ev, p0, p1).reshape(1)
+        if world > 1:
+            dist.all_reduce(e)
+        out["e"] = e
+
+    N.launch_count = 0
+    ms, clocks = timed_steps(step, steps, warmup, world, gpu)
+    launches = N.launch_count // (steps + warmup) * steps
+    E = float(out["e"].item())
+    npairs = p1 - p0
+    sym_flops = nocc * (nocc + 1) / 2 * 2.0 * nvir * nvir * naux
+    # kernel-level: the fused kernel on this rank's range, timed alone
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    energy.pair_range_energy(B, eo, ev, p0, p1)
+    e_ev.record()
+    torch.cuda.synchronize()
+    kern_ms = s_ev.elapsed_time(e_ev)
+    # int8 pipe: units x 2 passes x (sum of MMA N) x 128 rows x naux_p x 2 ops
+    nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
+    upp = sum(max(0, nC - 2 * r) for r in range(nR))
+    naux_p = math.ceil(naux / 32) * 32
+    int8_ops = npairs * upp * 2 * (5 * 64 + 4 * 64 + 3 * 64 + 2 * 64 + 64) * 128 * naux_p * 2.0
+    pk, src = peaks()
+    int8_peak = 2 * pk["bf16_tflops_sustained"] * 2  # int8 dense = 2x bf16 (ops)
+    del B
+    torch.cuda.empty_cache()
+    return {
+        "ms_per_step": round(ms, 3),
+        "energy": E,
+        "tflops_sym_count": round(sym_flops / (ms / 1e3) / 1e12, 2),
+        "clocks": clocks,
+        "gpu_launches": launches,
+        "kernel_ms_alone": round(kern_ms, 3),
+        "int8_tops_achieved": round(int8_ops / (kern_ms / 1e3) / 1e12, 1),
+        "int8_peak_tops": int8_peak,
+        "int8_frac": round(int8_ops / (kern_ms / 1e3) / 1e12 / int8_peak, 4),
+        "peak_source": f"{src}: 2 x bf16 sustained TFLOP/s (int8 dense rate), in int8 ops",
+        "pairs_per_rank": npairs,
+        "config": {"nocc": nocc, "nvir": nvir, "naux": naux, "sharding": "i<=j pair ranges by count"},
+    }
+
+
+# ── main ─────────────────────────────────────────────────────────────────────
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="spmd",
+                    choices=["spmd", "gemm_fp32", "gemm8192_bf16", "gemm8192_fp32", "pair3", "pair5",
+                             "gemm_fp64", "batched", "syrk"])
+    ap.add_argument("--no-pair", action="store_true", help="skip the pair-energy block of the default line")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = setup_dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps(reference_arm(args, world)), flush=True)
+            return
+        line = run_ours(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+def run_ours(args, rank, world, gpu):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    if args.workload in ("spmd", "gemm_fp32"):
+        dt = torch.bfloat16 if args.workload == "spmd" else torch.float32
+        line = run_gemm_spmd(args, rank, world, gpu, dt)
+        if args.workload == "spmd" and not args.no_pair:
+            line["pair_energy"] = run_pair(args, rank, world, gpu, 96, 2208, 6912, steps=2, warmup=1)
+            line["pair_energy"]["metric"] = "DF-MP2 pair-energy step ms (config 5: 96/2208/6912)"
+        if rank == 0:
+            line["cpu_baseline"] = cpu_baseline_gemm(dt) if world == 1 else None
+        return line
+    if args.workload in ("pair3", "pair5"):
+        dims = (48, 432, 1152) if args.workload == "pair3" else (96, 2208, 6912)
+        r = run_pair(args, rank, world, gpu, *dims)
+        line = {
+            "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
+            "value": r["ms_per_step"], "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 (5 Ozaki slices, exact int32) + fp64 reduction",
+            "data": "synthetic (BASELINE recipe, device generator)",
+            "config": {"workload": args.workload, **r["config"]},
+            "roofline": {"bound": "tensor", "achieved": r["int8_tops_achieved"], "peak": r["int8_peak_tops"],
+                         "unit": "TOP/s (int8)", "frac": r["int8_frac"], "traffic": read_traffic(f"pair_energy_{args.workload}")},
+            "clocks": r["clocks"], "gpu_launches": r["gpu_launches"], "detail": r,
+        }
+        if rank == 0 and world == 1:
+            ms, th, sample = cpu_pair_sample(*dims)
+            line["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample}
+        return line
+    return run_single(args, rank, world, gpu)
+
+
+def cpu_baseline_gemm(dt):
+    v, th, sample = cpu_gemm_sample(32768, dt)
+    return {"value": round(v, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
+            "sample": sample + " (torch CPU matmul: the reference's host route)"}
+
+
+def run_single(args, rank, world, gpu):
+    """Single-GPU workloads (each rank runs its own replica)."""
+    import trnblas_b200 as tb
+    from trnblas_b200 import _native as N
+
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    wl = args.workload
+    if wl.startswith("gemm8192"):
+        dt = torch.bfloat16 if wl.endswith("bf16") else torch.float32
+        n = 8192
+        A = torch.randn(n, n, device="cuda", generator=g).to(dt)
+        B = torch.randn(n, n, device="cuda", generator=g).to(dt)
+        fn = lambda: tb.gemm(1.0, A, B)  # noqa: E731
+        flops = 2.0 * n ** 3
+    elif wl == "batched":
+        A = torch.randn(64, 512, 512, device="cuda", generator=g)
+        B = torch.randn(64, 512, 512, device="cuda", generator=g)
+        fn = lambda: tb.batched_gemm(1.0, A, B)  # noqa: E731
+        flops = 64 * 2.0 * 512 ** 3
+    elif wl == "syrk":
+        A = torch.randn(4096, 4096, device="cuda", generator=g) / 64
+        fn = lambda: tb.syrk(1.0, A, uplo="lower")  # noqa: E731
+        flops = 4096 * 4097 * 4096.0
+    else:  # gemm_fp64, config 4
+        n = 4096
+        A = torch.randn(n, n, device="cuda", dtype=torch.float64, generator=g) * torch.exp2(
+            torch.randint(-10, 11, (n, n), device="cuda", generator=g).double())
+        B = torch.randn(n, n, device="cuda", dtype=torch.float64, generator=g) * torch.exp2(
+            torch.randint(-10, 11, (n, n), device="cuda", generator=g).double())
+        fn = lambda: tb.gemm_fp64(A, B)  # noqa: E731
+        flops = 2.0 * n ** 3
+    N.launch_count = 0
+    ms, clocks = timed_steps(fn, args.steps, args.warmup, world, gpu)
+    launches = N.launch_count // (args.steps + args.warmup) * args.steps
+    value = flops / (ms / 1e3) / 1e12 * world
+    return {"metric": f"{wl} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": str(A.dtype).split(".")[-1],
+            "data": "synthetic (seeded, device generator)", "config": {"workload": wl, "replicas": world},
+            "clocks": clocks, "gpu_launches": launches}
+
+
+def reference_arm(args, world):
+    """The reference's CPU route (restated in oracle/ and torch CPU), bounded sample."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    if args.workload in ("pair3", "pair5"):
+        dims = (48, 432, 1152) if args.workload == "pair3" else (96, 2208, 6912)
+        ms, th, sample = cpu_pair_sample(*dims, budget_s=8.0)
+        return {"impl": "reference", "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
+                "value": round(ms, 1), "unit": "ms", "higher_is_better": False, "n_gpus": world,
+                "steps": 1, "warmup": 1, "config": {"workload": args.workload},
+                "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample},
+                "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    dt = torch.float32 if args.workload in ("gemm_fp32", "gemm8192_fp32") else torch.bfloat16
+    n = 32768 if args.workload in ("spmd", "gemm_fp32") else 8192
+    vals = []
+    for _ in range(max(1, min(args.steps, 2))):
+        v, th, sample = cpu_gemm_sample(n, dt, budget_s=8.0)
+        vals.append(v)
+    v = statistics.median(vals)
+    return {"impl": "reference", "metric": f"GEMM TFLOP/s (M=N=K={n}, {str(dt).split('.')[-1]})",
+            "value": round(v, 4), "unit": "TFLOP/s", "higher_is_better": True, "n_gpus": world,
+            "steps": len(vals), "warmup": 1, "config": {"workload": args.workload, "M": n, "N": n, "K": n},
+            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
+                             "sample": sample + " (torch CPU matmul: the reference's host route)"},
+            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+if __name__ == "__main__":
+    main()

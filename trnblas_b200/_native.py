@@ -80,6 +80,15 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+# Kernels launched through this binding (for the benchmark's launch count).
+launch_count = 0
+
+
+def count_launches(n: int) -> None:
+    global launch_count
+    launch_count += int(n)
+
+
 def last_error() -> str:
     msg = lib().trnblas_last_error()
     return msg.decode() if msg else ""

@@ -107,6 +107,7 @@ def _gemm2d(a: torch.Tensor, b: torch.Tensor, alpha: float, beta: float, C) -> t
         N.ptr(ws), ws_bytes, N.stream_ptr(dev),
     )
     N.check(rc, "trnblas_gemm")
+    N.count_launches(3 if code == N.F32 and K > 0 else 1)  # (2 split kernels +) GEMM
     return out
 
 
@@ -292,6 +293,7 @@ def _batched(alpha, a, b, beta, C):
             N.ptr(ws), ws_bytes, N.stream_ptr(dev),
         )
         N.check(rc, "trnblas_gemm (batched)")
+        N.count_launches(3 if code == N.F32 and K > 0 else 1)
         r = out
     if not fuse:
         r = _add_c(r, beta, Cd)
@@ -371,6 +373,7 @@ def _syrk_kernel(a_eff: torch.Tensor, alpha: float, beta: float, C, c_uplo: int)
         N.ptr(out), n, N.ptr(ws), ws_bytes, N.stream_ptr(dev),
     )
     N.check(rc, "trnblas_syrk")
+    N.count_launches(2 if code == N.F32 else 1)
     return out
 
 
@@ -470,6 +473,7 @@ def _gemm_fp64_device(a: torch.Tensor, b: torch.Tensor, k: int) -> torch.Tensor:
         N.ptr(out), Nn, N.ptr(ws), ws_bytes, N.stream_ptr(dev),
     )
     N.check(rc, "trnblas_gemm_fp64")
+    N.count_launches(8 + 1)  # two 4-kernel splits + the int8 GEMM (one K block)
     return out
 
 

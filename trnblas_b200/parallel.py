@@ -167,6 +167,7 @@ def gemm_2d(
     B_shard: torch.Tensor,
     grid: Grid2D,
     k_chunks: int = 4,
+    kernel_events: list | None = None,
 ) -> torch.Tensor:
     """This rank's (M/pr) x (N/pc) block of C = A @ B on a pr x pc grid.
 
@@ -177,7 +178,9 @@ def gemm_2d(
     in `k_chunks` K-chunks on a side stream while the local GEMM of the
     previous chunk runs; chunk products accumulate through the fused beta = 1
     epilogue. Returns the C block (rows `grid.block_rows(M)`, columns
-    `grid.block_cols(N)`).
+    `grid.block_cols(N)`). A grid row / column of one rank needs no gather.
+    `kernel_events`, when given, receives a (start, end) CUDA event pair
+    around each local GEMM launch on the launching stream.
     """
     pr, pc = grid.pr, grid.pc
     mw, K = A_shard.shape
@@ -192,13 +195,19 @@ def gemm_2d(
     main = torch.cuda.current_stream(dev) if cuda else None
 
     def gather_chunk(k0, k1):
-        a_part = A_shard[:, k0:k1].contiguous()
-        a_full = torch.empty((pc * mw, k1 - k0), dtype=A_shard.dtype, device=dev)
-        dist.all_gather_into_tensor(a_full, a_part, group=grid.row_group)
-        b_part = B_shard[k0:k1].T.contiguous()  # (nw, kc)
-        b_full = torch.empty((pr * nw, k1 - k0), dtype=B_shard.dtype, device=dev)
-        dist.all_gather_into_tensor(b_full, b_part, group=grid.col_group)
-        return a_full, b_full  # b_full stores the B block transposed (N_blk, kc)
+        if pc == 1:
+            a_full = A_shard[:, k0:k1]
+        else:
+            a_part = A_shard[:, k0:k1].contiguous()
+            a_full = torch.empty((pc * mw, k1 - k0), dtype=A_shard.dtype, device=dev)
+            dist.all_gather_into_tensor(a_full, a_part, group=grid.row_group)
+        if pr == 1:
+            b_full = B_shard[k0:k1].T  # a transposed view: the kernel reads it as is
+        else:
+            b_part = B_shard[k0:k1].T.contiguous()  # (nw, kc)
+            b_full = torch.empty((pr * nw, k1 - k0), dtype=B_shard.dtype, device=dev)
+            dist.all_gather_into_tensor(b_full, b_part, group=grid.col_group)
+        return a_full, b_full  # b_full holds the B block transposed (N_blk, kc)
 
     C = None
     pending, events = [], []
@@ -226,7 +235,13 @@ def gemm_2d(
             part = _local_mm(a_full, b_full_t.T)
             C = part if C is None else C + part
         else:
+            if kernel_events is not None:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record(main)
             C = _gemm(1.0, a_full, b_full_t, 1.0 if C is not None else 0.0, C, transB=True)
+            if kernel_events is not None:
+                ev1.record(main)
+                kernel_events.append((ev0, ev1))
         pending[i] = None
     if C is None:
         C = torch.zeros((pc * mw, pr * nw), dtype=A_shard.dtype, device=dev)

@@ -79,6 +79,24 @@ TRNBLAS_API int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int
                  int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * fp32 GEMM (no batch) that allocates nothing: D = alpha * op(A) @ op(B) +
+ * beta * C with the argument meanings of trnblas_gemm, for callers that may
+ * not allocate device memory when they multiply (plugins whose host owns all
+ * device memory, loops where cudaMalloc's device synchronisation is not
+ * allowed). Its split scratch is a 64 MiB array built into the library and
+ * held on every GPU that loads it; problems with 2 * (M + N) * round_up(K, 4)
+ * * 4 bytes of split planes above that are rejected (TRNBLAS_ERR_WORKSPACE).
+ * The first call on a device looks up the array's address (make it before any
+ * stream capture). All calls on a device share the array: calls that may
+ * overlap on the GPU (other streams, other threads) race and must be
+ * serialised. No counterpart in the reference.
+ */
+TRNBLAS_API int trnblas_gemm_f32_noalloc(int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+                             int64_t lda, int transA, const float* B, int64_t ldb, int transB,
+                             float beta, const float* C, int64_t ldc, float* D, int64_t ldd,
+                             void* stream);
+
 /* Bytes of workspace trnblas_syrk needs (0 for bf16/fp16). */
 TRNBLAS_API size_t trnblas_syrk_workspace_size(int dtype, int64_t n, int64_t k);
 

@@ -37,6 +37,9 @@ _SIGNATURES = {
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
          _i64, _p, _i64, _i64, _p, _sz, _p],
     ),
+    "trnblas_gemm_f32_noalloc": (
+        _i, [_i64, _i64, _i64, _f, _p, _i64, _i, _p, _i64, _i, _f, _p, _i64, _p, _i64, _p]
+    ),
     "trnblas_syrk_workspace_size": (_sz, [_i, _i64, _i64]),
     "trnblas_syrk": (
         _i, [_i, _i64, _i64, _f, _p, _i64, _i, _f, _p, _i64, _i, _p, _i64, _p, _sz, _p]

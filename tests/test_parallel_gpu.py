@@ -1,0 +1,96 @@
+"""SPMD paths on NCCL across the visible GPUs (one spawned process per GPU;
+skipped with fewer than 2 GPUs): the reference's GEMM primitives, the 2-D
+output-block GEMM, and the pair-range energy with its single fp64 all-reduce,
+each against the full single-process result."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _relf(x, ref):
+    return float((x.double() - ref.double()).norm() / ref.double().norm())
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        import trnblas_b200 as tb
+        import trnblas_b200.parallel as tp
+        from oracle import pair_energy as PE
+
+        dev = torch.device("cuda", rank)
+        g = torch.Generator(device=dev).manual_seed(5)  # same full operands on every rank
+        n = 1024 * world
+        A = (2 * torch.rand(n, n, device=dev, generator=g) - 1)
+        B = (2 * torch.rand(n, n, device=dev, generator=g) - 1)
+        full = A.double() @ B.double()
+        grid = tp.Grid2D()
+        for dt, tol in ((torch.bfloat16, 1e-2), (torch.float32, 1e-5)):
+            As, Bs = tp.shard_2d(A.to(dt), B.to(dt), grid)
+            C = tp.gemm_2d(As.contiguous(), Bs.contiguous(), grid, k_chunks=3)
+            r0, r1 = grid.block_rows(n)
+            c0, c1 = grid.block_cols(n)
+            ref = (A.to(dt).double() @ B.to(dt).double())[r0:r1, c0:c1]
+            out[f"gemm2d_{dt}"] = _relf(C, ref) <= tol
+        mw = n // world
+        rows = tp.gemm_row_parallel(A[rank * mw:(rank + 1) * mw].contiguous(), B, gather=True)
+        cols = tp.gemm_col_parallel(A, B[:, rank * mw:(rank + 1) * mw].contiguous(), gather=True)
+        ksum = tp.gemm_k_parallel(A[:, rank * mw:(rank + 1) * mw].contiguous(), B[rank * mw:(rank + 1) * mw].contiguous())
+        kscat = tp.gemm_k_parallel(A[:, rank * mw:(rank + 1) * mw].contiguous(), B[rank * mw:(rank + 1) * mw].contiguous(), scatter=True)
+        out["row"] = _relf(rows, full) <= 1e-5
+        out["col"] = _relf(cols, full) <= 1e-5
+        out["k"] = _relf(ksum, full) <= 1e-5
+        out["kscatter"] = _relf(kscat, full[rank * mw:(rank + 1) * mw]) <= 1e-5
+        Bh, eo, ev = PE.make_inputs(9, 100, 64, 3)
+        E = tp.pair_energy(Bh.to(dev), eo.to(dev), ev.to(dev))
+        ref = PE.chunked_energy(Bh.numpy(), eo.numpy(), ev.numpy())
+        out["energy"] = abs(E - ref) <= 1e-9 * abs(ref)
+        out["E"] = E
+        out["status"] = tb.device_status(rank)
+    except Exception as e:  # reported to the parent
+        out["error"] = repr(e)
+    finally:
+        dist.destroy_process_group()
+    q.put((rank, out))
+
+
+def test_spmd_on_nccl():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert "error" not in res[r], res[r]
+        bad = [k for k, v in res[r].items() if v is False]
+        assert not bad, (r, bad)
+        assert res[r]["status"] == 0
+    assert len({res[r]["E"] for r in range(world)}) == 1

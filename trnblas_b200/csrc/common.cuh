@@ -162,6 +162,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Contiguous bulk copy global -> shared (no tensor map, no multicast):
+// 16-byte aligned addresses, size a multiple of 16, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tcgen05.mma / TMA store reads of data written by ordinary stores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -276,6 +287,19 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
   d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// K-major descriptor without swizzle: core matrices of 8 rows x 16 bytes
+// (128 contiguous bytes), the two 16-byte K halves of a 32-byte MMA K step
+// `lbo` apart, consecutive 8-row groups `sbo` apart.
+__device__ __forceinline__ uint64_t sdesc_kmajor_noswz(uint32_t saddr, uint32_t lbo_bytes,
+                                                       uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // sm_100 descriptor version; layout 0 = no swizzle
   return d;
 }
 

@@ -1,9 +1,12 @@
 // fp64-class GEMM by Ozaki splitting on the int8 tensor cores (kind::i8).
 //
 // op(A) (M x K) is split per row and op(B) (K x N) per column into `k`
-// balanced 7-bit digit planes (ozaki_split.cuh). For an output tile the K
-// loop stages all k A-planes (128 rows) and all k B-planes (BN rows, stacked
-// along N) of one 32-wide K slab per pipeline stage, then issues the slice
+// balanced 7-bit digit planes (ozaki_split.cuh), written in the tiled layout
+// that is the MMA's shared-memory image, so every (K slab, plane, row block)
+// tile is one contiguous chunk fetched by a plain bulk copy of whole 128-byte
+// lines. For an output tile the K loop stages all k A-planes (128 rows) and
+// all k B-planes (BN rows, stacked along N) of one 32-wide K slab per pipeline
+// stage, then issues the slice
 // products of every diagonal d = s + t <= k - 1 into int32 TMEM accumulators,
 // diagonal d at TMEM columns [d*BN, (d+1)*BN). Because the B-planes are
 // contiguous along N, one MMA of A-plane s against B-planes t0 .. t0+n-1
@@ -24,6 +27,9 @@
 namespace tb {
 
 struct OzParams {
+  const int8_t* dA;   // tiled digits of op(A): rows_a_pad rows
+  const int8_t* dB;   // tiled digits of op(B)^T: rows_b_pad rows
+  long long rows_a_pad, rows_b_pad;
   int M, N, Kp;       // Kp: K columns of the digit planes covered by this launch
   int k0;             // first K column of this launch (multiple of 32)
   int slices;
@@ -40,7 +46,7 @@ struct OzParams {
 template <int BN, int KSMAX>
 struct OzCfg {
   static constexpr int BM = 128;
-  static constexpr int BK = 32;                  // one 32-byte swizzle row of int8
+  static constexpr int BK = 32;                  // one 32-byte MMA K step of int8
   static constexpr int A_PLANE = BM * BK;        // bytes
   static constexpr int B_PLANE = BN * BK;
   static constexpr int STAGE_BYTES = KSMAX * (A_PLANE + B_PLANE);
@@ -50,8 +56,7 @@ struct OzCfg {
 
 template <int BN, int KSMAX, int STAGES>
 __global__ void __launch_bounds__(192, 1)
-    ozaki_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
-                      const __grid_constant__ CUtensorMap map_b, const OzParams p) {
+    ozaki_gemm_kernel(const OzParams p) {
   using Cfg = OzCfg<BN, KSMAX>;
   constexpr int BM = Cfg::BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -80,8 +85,6 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&map_a);
-    tma_prefetch_desc(&map_b);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
@@ -106,8 +109,14 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* sb = sa + KSMAX * Cfg::A_PLANE;
         mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
         const int kc = p.k0 + kb * Cfg::BK;
-        tma_load_3d(sa, &map_a, &full_bar[stage], kc, mb * BM, 0);
-        tma_load_3d(sb, &map_b, &full_bar[stage], kc, nb * BN, 0);
+        for (int s = 0; s < ks; ++s) {
+          bulk_load(sa + s * Cfg::A_PLANE,
+                    p.dA + tiled_offset(static_cast<long long>(mb) * BM, kc, s, ks, p.rows_a_pad),
+                    Cfg::A_PLANE, &full_bar[stage]);
+          bulk_load(sb + s * Cfg::B_PLANE,
+                    p.dB + tiled_offset(static_cast<long long>(nb) * BN, kc, s, ks, p.rows_b_pad),
+                    Cfg::B_PLANE, &full_bar[stage]);
+        }
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -147,11 +156,11 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
         const uint32_t sb = sa + KSMAX * Cfg::A_PLANE;
         for (int s = 0; s < ks; ++s) {
-          const uint64_t ad = sdesc_kmajor(sa + s * Cfg::A_PLANE, 256, kSwz32);
+          const uint64_t ad = sdesc_kmajor_noswz(sa + s * Cfg::A_PLANE, 128, 256);
           const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
           for (int t0 = 0; t0 < ks - s; t0 += Cfg::PLANES_PER_MMA) {
             const int np = min(Cfg::PLANES_PER_MMA, ks - s - t0);
-            const uint64_t bd = sdesc_kmajor(sb + t0 * Cfg::B_PLANE, 256, kSwz32);
+            const uint64_t bd = sdesc_kmajor_noswz(sb + t0 * Cfg::B_PLANE, 128, 256);
             const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, BM, np * BN);
             mma_i8(tmem_base + (s + t0) * BN, ad, bd, id, acc_in);
           }
@@ -232,8 +241,7 @@ __global__ void __launch_bounds__(192, 1)
 namespace {
 
 template <int BN, int KSMAX, int STAGES>
-int launch_oz(const CUtensorMap& ma, const CUtensorMap& mb, const OzParams& p,
-              cudaStream_t stream) {
+int launch_oz(const OzParams& p, cudaStream_t stream) {
   constexpr int smem = STAGES * OzCfg<BN, KSMAX>::STAGE_BYTES + 1024 + 256;
   auto kern = ozaki_gemm_kernel<BN, KSMAX, STAGES>;
   static bool attr_set[64] = {};
@@ -244,13 +252,14 @@ int launch_oz(const CUtensorMap& ma, const CUtensorMap& mb, const OzParams& p,
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int grid = static_cast<int>(std::min<long long>(p.num_tiles, num_sms()));
-  kern<<<grid, 192, smem, stream>>>(ma, mb, p);
+  kern<<<grid, 192, smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "ozaki kernel launch");
 }
 
 struct OzLayout {
   long long kp;        // K padded to 32 (digit plane row length)
+  long long ma, nb;    // rows of the tiled A (multiple of 128) and B (multiple of 64)
   size_t dig_a, dig_b; // bytes
   size_t off_dig_b, off_exp_a, off_exp_b, off_max, off_range, total;
 };
@@ -258,8 +267,10 @@ struct OzLayout {
 OzLayout oz_layout(long long M, long long N, long long K, int slices) {
   OzLayout L{};
   L.kp = round_up(std::max<long long>(K, 1), 32);
-  L.dig_a = static_cast<size_t>(round_up(slices * M * L.kp, 256));
-  L.dig_b = static_cast<size_t>(round_up(slices * N * L.kp, 256));
+  L.ma = round_up(std::max<long long>(M, 1), 128);
+  L.nb = round_up(std::max<long long>(N, 1), 64);
+  L.dig_a = static_cast<size_t>(round_up(slices * L.ma * L.kp, 256));
+  L.dig_b = static_cast<size_t>(round_up(slices * L.nb * L.kp, 256));
   L.off_dig_b = L.dig_a;
   L.off_exp_a = L.off_dig_b + L.dig_b;
   L.off_exp_b = L.off_exp_a + round_up(4 * M, 256);
@@ -356,31 +367,22 @@ int trnblas_gemm_fp64(int64_t M, int64_t N, int64_t K, const double* A, int64_t 
   // op(A)(m, k): strides; op(B)^T(n, k) = op(B)(k, n)
   const long long ars = transA ? 1 : lda, aks = transA ? lda : 1;
   const long long brs = transB ? ldb : 1, bks = transB ? 1 : ldb;
-  cudaError_t e = launch_split(A, ars, aks, static_cast<int>(M), static_cast<int>(K),
-                               static_cast<int>(L.kp), slices, dA, eA, sc, stream);
+  // one group of M (N) real rows padded to L.ma (L.nb): padding rows are zero
+  cudaError_t e = launch_split_tiled(A, ars, aks, static_cast<int>(M), static_cast<int>(K), M,
+                                     L.ma, L.ma, static_cast<int>(L.kp), slices, dA, eA, sc,
+                                     stream);
   if (e == cudaSuccess)
-    e = launch_split(B, brs, bks, static_cast<int>(N), static_cast<int>(K),
-                     static_cast<int>(L.kp), slices, dB, eB, sc, stream);
+    e = launch_split_tiled(B, brs, bks, static_cast<int>(N), static_cast<int>(K), N, L.nb, L.nb,
+                           static_cast<int>(L.kp), slices, dB, eB, sc, stream);
   if (e != cudaSuccess) return cuda_fail(e, "ozaki split launch");
 
   const bool wide = slices <= 8;  // BN = 64 holds 8 diagonals; 9..12 use BN = 32
   const int BN = wide ? 64 : 32;
-  CUtensorMap ma, mb;
-  const uint64_t dims_a[3] = {static_cast<uint64_t>(L.kp), static_cast<uint64_t>(M),
-                              static_cast<uint64_t>(slices)};
-  const uint64_t str_a[2] = {static_cast<uint64_t>(L.kp), static_cast<uint64_t>(M * L.kp)};
-  const uint32_t box_a[3] = {32, 128, static_cast<uint32_t>(slices)};
-  const uint64_t dims_b[3] = {static_cast<uint64_t>(L.kp), static_cast<uint64_t>(N),
-                              static_cast<uint64_t>(slices)};
-  const uint64_t str_b[2] = {static_cast<uint64_t>(L.kp), static_cast<uint64_t>(N * L.kp)};
-  const uint32_t box_b[3] = {32, static_cast<uint32_t>(BN), static_cast<uint32_t>(slices)};
-  if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dA, 3, dims_a, str_a, box_a,
-                  CU_TENSOR_MAP_SWIZZLE_32B) ||
-      !encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dB, 3, dims_b, str_b, box_b,
-                  CU_TENSOR_MAP_SWIZZLE_32B))
-    return TRNBLAS_ERR_ALIGN;
-
   OzParams p{};
+  p.dA = dA;
+  p.dB = dB;
+  p.rows_a_pad = L.ma;
+  p.rows_b_pad = L.nb;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.slices = slices;
@@ -398,8 +400,7 @@ int trnblas_gemm_fp64(int64_t M, int64_t N, int64_t K, const double* A, int64_t 
     p.k0 = static_cast<int>(k0);
     p.Kp = static_cast<int>(std::min(kbmax, L.kp - k0));
     p.accumulate = k0 > 0;
-    const int rc = wide ? launch_oz<64, 8, 4>(ma, mb, p, stream)
-                        : launch_oz<32, 12, 3>(ma, mb, p, stream);
+    const int rc = wide ? launch_oz<64, 8, 4>(p, stream) : launch_oz<32, 12, 3>(p, stream);
     if (rc) return rc;
   }
   return TRNBLAS_OK;

@@ -134,6 +134,109 @@ __global__ void ozk_digits_kernel(const T* __restrict__ X, long long rs, long lo
   }
 }
 
+// Tiled digit layout: the image the int8 MMA reads from shared memory, so a
+// tile of any 8-aligned row range of one plane and one 32-wide K slab is one
+// contiguous chunk (fetched with a single bulk copy of whole 128-byte lines):
+//   [K slab (32)][plane][8-row group][K half (16)][row in group (8)][16 bytes]
+// i.e. no-swizzle K-major core matrices (8 rows x 16 bytes), LBO = 128 bytes
+// between the K halves, SBO = 256 bytes between row groups.
+__host__ __device__ __forceinline__ long long tiled_offset(long long p, int k, int s, int slices,
+                                                           long long rows_pad) {
+  const long long slab = k >> 5;
+  const int kk = k & 31;
+  return ((((slab * slices + s) * (rows_pad >> 3) + (p >> 3)) * 2 + (kk >> 4)) << 7) +
+         ((p & 7) << 4) + (kk & 15);
+}
+
+// Digits in the tiled layout. Padded row p maps to logical row
+// (p / gp) * g + p % gp when p % gp < g (else the row is zero padding): the
+// pair energy pads each occupied orbital's nvir rows to a multiple of 128, the
+// GEMM pads the end. 32 x 32 tiles; digits staged in shared memory, then
+// written 16 bytes at a time.
+template <typename T>
+__global__ void ozk_digits_tiled_kernel(const T* __restrict__ X, long long rs, long long ks,
+                                        int K, long long g, long long gp, long long rows_pad,
+                                        int kpad, int slices, const int* __restrict__ exps,
+                                        const int* __restrict__ shift_range,
+                                        int8_t* __restrict__ digits) {
+  __shared__ double tile[32][33];
+  __shared__ __align__(16) int8_t dg[12][32][32];
+  const int k0 = blockIdx.x * 32;
+  const long long p0 = static_cast<long long>(blockIdx.y) * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  auto src_row = [&](long long p) -> long long {
+    const long long q = p / gp, a = p - q * gp;
+    return (a < g) ? q * g + a : -1;
+  };
+  if (ks == 1) {
+    for (int i = ty; i < 32; i += 8) {
+      const long long r = src_row(p0 + i);
+      const int k = k0 + tx;
+      tile[i][tx] = (r >= 0 && k < K) ? static_cast<double>(__ldg(X + r * rs + k)) : 0.0;
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const long long r = src_row(p0 + tx);
+      const int k = k0 + i;
+      tile[tx][i] = (r >= 0 && k < K) ? static_cast<double>(__ldg(X + r * rs + k * ks)) : 0.0;
+    }
+  }
+  __syncthreads();
+  const bool two = shift_range[0] > 1023 || shift_range[1] < -1022;
+  for (int i = ty; i < 32; i += 8) {
+    const long long r = src_row(p0 + i);
+    double v = tile[i][tx];
+    if (r >= 0 && v != 0.0) {
+      const int shift = 6 - exps[r];
+      if (!two) {
+        v = v * pow2d(shift);
+      } else {
+        const int h = (shift >= 0) ? shift / 2 : -((-shift + 1) / 2);
+        v = v * pow2d(h);
+        v = v * pow2d(shift - h);
+      }
+    }
+    for (int s = 0; s < slices; ++s) {
+      if (s) v = v * 128.0;
+      const double d = rint(v);
+      if (s + 1 < slices) v = v - d;
+      dg[s][i][tx] = static_cast<int8_t>(static_cast<int>(d));
+    }
+  }
+  __syncthreads();
+  // 16-byte stores: (plane, row, K half) items
+  const int t = ty * 32 + tx;
+  for (int it = t; it < slices * 64; it += 256) {
+    const int s = it >> 6, row = (it >> 1) & 31, half = it & 1;
+    const long long off = tiled_offset(p0 + row, k0 + 16 * half, s, slices, rows_pad);
+    *reinterpret_cast<uint4*>(digits + off) = *reinterpret_cast<const uint4*>(&dg[s][row][16 * half]);
+  }
+}
+
+// Split into the tiled layout: R logical rows (row r at X[r * rs + k * ks]),
+// rows_pad padded rows grouped as described above, K padded to kpad (multiple
+// of 32). scratch as for launch_split.
+template <typename T>
+inline cudaError_t launch_split_tiled(const T* X, long long rs, long long ks, int R, int K,
+                                      long long g, long long gp, long long rows_pad, int kpad,
+                                      int slices, int8_t* digits, int* exps,
+                                      SplitScratch scratch, cudaStream_t stream) {
+  if ((R + 31) / 32 > 65535 || rows_pad / 32 > 65535 || (rows_pad & 31) || (kpad & 31) ||
+      slices > 12)
+    return cudaErrorInvalidConfiguration;
+  ozk_init_kernel<<<(R + 255) / 256 + 1, 256, 0, stream>>>(scratch.maxbits, R,
+                                                          scratch.shift_range);
+  dim3 blk(32, 8);
+  dim3 g1(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((R + 31) / 32));
+  if (K > 0) ozk_rowmax_kernel<T><<<g1, blk, 0, stream>>>(X, rs, ks, R, K, scratch.maxbits);
+  ozk_exps_kernel<<<(R + 255) / 256, 256, 0, stream>>>(scratch.maxbits, R, exps,
+                                                       scratch.shift_range);
+  dim3 g3(static_cast<unsigned>(kpad / 32), static_cast<unsigned>(rows_pad / 32));
+  ozk_digits_tiled_kernel<T><<<g3, blk, 0, stream>>>(X, rs, ks, K, g, gp, rows_pad, kpad, slices,
+                                                     exps, scratch.shift_range, digits);
+  return cudaGetLastError();
+}
+
 // Run the passes on `stream`. scratch.maxbits (R words) and
 // scratch.shift_range (2 ints) are initialised here.
 template <typename T>

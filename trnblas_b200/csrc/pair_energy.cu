@@ -43,6 +43,9 @@
 namespace tb {
 
 struct PairParams {
+  const int8_t* digits;    // tiled digit planes, rows (i, a) at i * nv_pad + a
+  long long rows_pad;      // nocc * nv_pad
+  int nv_pad;              // nvir rounded up to 128 (zero rows beyond nvir)
   int nocc, nvir, naux_p;  // naux_p: K columns of the digit planes (multiple of 32)
   long long pair_begin;
   long long num_units;     // pairs * units_per_pair
@@ -96,8 +99,7 @@ __device__ __forceinline__ float pow2f(int n) {
 
 template <int KS, int STAGES>
 __global__ void __launch_bounds__(192, 1)
-    pair_energy_kernel(const __grid_constant__ CUtensorMap map_rows128,
-                       const __grid_constant__ CUtensorMap map_rows64, const PairParams p) {
+    pair_energy_kernel(const PairParams p) {
   using Cfg = PairCfg<KS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -125,8 +127,6 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     for (int w = 0; w < 4; ++w) red[w] = 0.0;
     fence_barrier_init();
-    tma_prefetch_desc(&map_rows128);
-    tma_prefetch_desc(&map_rows64);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
@@ -143,10 +143,11 @@ __global__ void __launch_bounds__(192, 1)
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
       int i, j, R, C;
       unit_of(p, u, i, j, R, C);
-      const int ri = i * p.nvir, rj = j * p.nvir;
+      const long long ri = static_cast<long long>(i) * p.nv_pad;
+      const long long rj = static_cast<long long>(j) * p.nv_pad;
       for (int pass = 0; pass < 2 && !aborted; ++pass) {
-        const int ra = (pass == 0 ? ri : rj) + 128 * R;  // A rows: B_i[R] then B_j[R]
-        const int rb = (pass == 0 ? rj : ri) + 64 * C;   // B rows: B_j[C] then B_i[C]
+        const long long ra = (pass == 0 ? ri : rj) + 128 * R;  // A rows: B_i[R] then B_j[R]
+        const long long rb = (pass == 0 ? rj : ri) + 64 * C;   // B rows: B_j[C] then B_i[C]
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
             aborted = true;
@@ -155,8 +156,15 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           const int kc = kb * Cfg::BK;
-          tma_load_3d(st + Cfg::A_OFF, &map_rows128, &full_bar[stage], kc, ra, 0);
-          tma_load_3d(st + Cfg::B_OFF, &map_rows64, &full_bar[stage], kc, rb, 0);
+#pragma unroll
+          for (int s = 0; s < KS; ++s) {
+            bulk_load(st + Cfg::A_OFF + s * Cfg::A_PLANE,
+                      p.digits + tiled_offset(ra, kc, s, KS, p.rows_pad), Cfg::A_PLANE,
+                      &full_bar[stage]);
+            bulk_load(st + Cfg::B_OFF + s * Cfg::B_PLANE,
+                      p.digits + tiled_offset(rb, kc, s, KS, p.rows_pad), Cfg::B_PLANE,
+                      &full_bar[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -202,13 +210,14 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int s = 0; s < KS; ++s) {
             const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
-            const uint64_t ad = sdesc_kmajor(st + Cfg::A_OFF + s * Cfg::A_PLANE, 256, kSwz32);
+            const uint64_t ad = sdesc_kmajor_noswz(st + Cfg::A_OFF + s * Cfg::A_PLANE, 128, 256);
 #pragma unroll
             for (int t0 = 0; t0 < KS - s; t0 += 4) {
               const int np = (KS - s - t0 < 4) ? KS - s - t0 : 4;
               const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, 128, np * Cfg::BN);
               mma_i8(tmem_base + (s + t0) * Cfg::BN, ad,
-                     sdesc_kmajor(st + Cfg::B_OFF + t0 * Cfg::B_PLANE, 256, kSwz32), id, acc_in);
+                     sdesc_kmajor_noswz(st + Cfg::B_OFF + t0 * Cfg::B_PLANE, 128, 256), id,
+                     acc_in);
             }
           }
           tc_commit(&empty_bar[stage]);
@@ -334,7 +343,7 @@ constexpr int kPairStages = 6;
 constexpr int kMaxGrid = 1024;
 
 struct PairLayout {
-  long long naux_p, R;
+  long long naux_p, R, nv_pad, rows_pad;
   size_t off_exps, off_max, off_range, off_part, total;
 };
 
@@ -342,7 +351,9 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
   PairLayout L{};
   L.naux_p = round_up(std::max<long long>(naux, 1), 32);
   L.R = nocc * nvir;
-  const size_t dig = static_cast<size_t>(round_up(kPairSlices * L.R * L.naux_p, 256));
+  L.nv_pad = round_up(std::max<long long>(nvir, 1), 128);
+  L.rows_pad = nocc * L.nv_pad;
+  const size_t dig = static_cast<size_t>(round_up(kPairSlices * L.rows_pad * L.naux_p, 256));
   L.off_exps = dig;
   L.off_max = L.off_exps + round_up(4 * L.R, 256);
   L.off_range = L.off_max + round_up(8 * L.R, 256);
@@ -388,8 +399,8 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
     set_error("trnblas_pair_energy: NULL energy pointer");
     return TRNBLAS_ERR_ARG;
   }
-  if (nocc * nvir > (1ll << 31) - 1 - 128) {
-    set_error("trnblas_pair_energy: nocc * nvir must stay below 2^31");
+  if (nocc * round_up(std::max<int64_t>(nvir, 1), 128) > 65535ll * 32) {
+    set_error("trnblas_pair_energy: nocc * round_up(nvir, 128) must stay below 2097120");
     return TRNBLAS_ERR_ARG;
   }
   if (naux > ((1ll << 31) - 1) / (kPairSlices * 4096ll)) {
@@ -421,24 +432,15 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   SplitScratch sc{reinterpret_cast<unsigned long long*>(ws + L.off_max),
                   reinterpret_cast<int*>(ws + L.off_range)};
   double* partials = reinterpret_cast<double*>(ws + L.off_part);
-  cudaError_t e = launch_split(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
-                               static_cast<int>(L.naux_p), kPairSlices, dig, exps, sc, stream);
+  cudaError_t e = launch_split_tiled(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
+                                     nvir, L.nv_pad, L.rows_pad, static_cast<int>(L.naux_p),
+                                     kPairSlices, dig, exps, sc, stream);
   if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
 
-  CUtensorMap m128, m64;
-  const uint64_t dims[3] = {static_cast<uint64_t>(L.naux_p), static_cast<uint64_t>(L.R),
-                            static_cast<uint64_t>(kPairSlices)};
-  const uint64_t strides[2] = {static_cast<uint64_t>(L.naux_p),
-                               static_cast<uint64_t>(L.R * L.naux_p)};
-  const uint32_t box128[3] = {32, 128, kPairSlices};
-  const uint32_t box64[3] = {32, 64, kPairSlices};
-  if (!encode_map(&m128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 3, dims, strides, box128,
-                  CU_TENSOR_MAP_SWIZZLE_32B) ||
-      !encode_map(&m64, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 3, dims, strides, box64,
-                  CU_TENSOR_MAP_SWIZZLE_32B))
-    return TRNBLAS_ERR_ALIGN;
-
   PairParams p{};
+  p.digits = dig;
+  p.rows_pad = L.rows_pad;
+  p.nv_pad = static_cast<int>(L.nv_pad);
   p.nocc = static_cast<int>(nocc);
   p.nvir = static_cast<int>(nvir);
   p.naux_p = static_cast<int>(L.naux_p);
@@ -463,7 +465,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<grid, 192, smem, stream>>>(m128, m64, p);
+  kern<<<grid, 192, smem, stream>>>(p);
   pair_energy_finish<<<1, 32, 0, stream>>>(partials, grid, energy);
   e = cudaGetLastError();
   return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "pair energy launch");

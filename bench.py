@@ -524,11 +524,72 @@ def run_single(args, rank, world, gpu):
     ms, clocks = timed_steps(fn, args.steps, args.warmup, world, gpu)
     launches = N.launch_count // (args.steps + args.warmup) * args.steps
     value = flops / (ms / 1e3) / 1e12 * world
-    return {"metric": f"{wl} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+    line = {"metric": f"{wl} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": str(A.dtype).split(".")[-1],
             "data": "synthetic (seeded, device generator)", "config": {"workload": wl, "replicas": world},
             "clocks": clocks, "gpu_launches": launches}
+    line["roofline"] = single_roofline(wl, A, B, flops)
+    return line
+
+
+def single_roofline(wl, A, B, flops):
+    """Roofline of the library call alone (device time between CUDA events on
+    the launching stream, no host checks): gemm_fp64 against the int8 tensor
+    pipe (k (k + 1) / 2 int8 slice products, the split included in the time),
+    the others against the bf16 / 3xTF32 tensor rate."""
+    import trnblas_b200 as tb
+    from trnblas_b200 import level3
+
+    pk, src = peaks()
+    if wl == "gemm_fp64":
+        k = level3.DEFAULT_SLICES
+        call = lambda: level3._gemm_fp64_device(A, B, k)  # noqa: E731
+    elif wl.startswith("gemm8192"):
+        call = lambda: tb.gemm(1.0, A, B)  # noqa: E731
+    elif wl == "batched":
+        call = lambda: tb.batched_gemm(1.0, A, B)  # noqa: E731
+    else:
+        call = lambda: tb.syrk(1.0, A, uplo="lower")  # noqa: E731
+    for _ in range(2):
+        call()
+    reps = 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps):
+        call()
+    e.record()
+    torch.cuda.synchronize()
+    kms = s.elapsed_time(e) / reps
+    if wl == "gemm_fp64":
+        M, K = A.shape
+        ops = k * (k + 1) / 2 * 2.0 * M * B.shape[1] * K
+        achieved = ops / (kms / 1e3) / 1e12
+        peak = 2.0 * pk["bf16_tflops"]
+        # context: cuBLAS DGEMM (torch.matmul fp64) on the same operands
+        torch.matmul(A, B)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            torch.matmul(A, B)
+        e.record()
+        torch.cuda.synchronize()
+        dgemm = flops / (s.elapsed_time(e) / reps / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TOP/s (int8)",
+                "frac": round(achieved / peak, 4), "traffic": read_traffic("ozaki_fp64_4096"),
+                "kernel": "ozk split + ozaki_gemm_kernel (one trnblas_gemm_fp64 call)",
+                "kernel_ms": round(kms, 4), "fp64_tflops_of_call": round(flops / (kms / 1e3) / 1e12, 2),
+                "cublas_dgemm_tflops": round(dgemm, 2),
+                "peak_source": f"{src}: 2 x bf16 burst (int8 dense rate = 2 x bf16), int8 ops"}
+    bf16 = A.dtype == torch.bfloat16
+    peak = pk["bf16_tflops"] if bf16 else pk["bf16_tflops"] / 6.0
+    achieved = flops / (kms / 1e3) / 1e12
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": read_traffic("gemm_bf16_8192" if bf16 else "gemm_fp32_8192") if wl.startswith("gemm8192") else None,
+            "kernel_ms": round(kms, 4),
+            "peak_source": f"{src} bf16 burst" + ("" if bf16 else " / 6 (3 tf32 products at half the bf16 rate)")}
 
 
 def reference_arm(args, world):

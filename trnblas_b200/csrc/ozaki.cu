@@ -1,10 +1,10 @@
 // fp64-class GEMM by Ozaki splitting on the int8 tensor cores (kind::i8).
 //
 // op(A) (M x K) is split per row and op(B) (K x N) per column into `k`
-// balanced 7-bit digit planes (ozaki_split.cuh), written in the tiled layout
-// that is the MMA's shared-memory image, so every (K slab, plane, row block)
-// tile is one contiguous chunk fetched by a plain bulk copy of whole 128-byte
-// lines. For an output tile the K loop stages all k A-planes (128 rows) and
+// balanced 7-bit digit planes (ozaki_split.cuh), written in the blocked layout
+// that is the MMA's shared-memory image, so all k planes of one row block of
+// one K slab are one contiguous chunk: a pipeline stage is two bulk copies.
+// For an output tile the K loop stages all k A-planes (128 rows) and
 // all k B-planes (BN rows, stacked along N) of one 32-wide K slab per pipeline
 // stage, then issues the slice
 // products of every diagonal d = s + t <= k - 1 into int32 TMEM accumulators,
@@ -52,7 +52,52 @@ struct OzCfg {
   static constexpr int STAGE_BYTES = KSMAX * (A_PLANE + B_PLANE);
   static_assert(KSMAX * BN <= 512, "diagonal accumulators must fit TMEM");
   static constexpr int PLANES_PER_MMA = 256 / BN;
+  static constexpr int BN_LOG2 = BN == 64 ? 6 : 5;
+  static_assert(BN == 64 || BN == 32, "B row blocks of 32 or 64 rows");
 };
+
+// MMA issuer role for exactly KS slices (compile time): every product of
+// diagonal d = s + t <= KS - 1 of each K slab, A-plane s against B-planes
+// t0 .. t0 + np - 1 stacked along N, into TMEM columns (s + t0) * BN.
+template <int BN, int KSMAX, int STAGES, int KS>
+__device__ __forceinline__ void oz_mma_role(const OzParams& p, uint8_t* smem, uint64_t* full_bar,
+                                            uint64_t* empty_bar, uint64_t* accf_bar,
+                                            uint64_t* acce_bar, uint32_t tmem_base, int num_kb,
+                                            const Abort& ab) {
+  using Cfg = OzCfg<BN, KSMAX>;
+  constexpr int PPM = Cfg::PLANES_PER_MMA;
+  int stage = 0;
+  uint32_t phase = 0;
+  int it = 0;
+  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+    if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) return;
+    tc_fence_after();
+    for (int kb = 0; kb < num_kb; ++kb) {
+      if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) return;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+      const uint32_t sb = sa + KSMAX * Cfg::A_PLANE;
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const uint64_t ad = sdesc_kmajor_noswz(sa + s * Cfg::A_PLANE, 128, 256);
+        const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
+#pragma unroll
+        for (int t0 = 0; t0 < KS - s; t0 += PPM) {
+          const int np = (KS - s - t0 < PPM) ? KS - s - t0 : PPM;
+          mma_i8(tmem_base + (s + t0) * BN, ad,
+                 sdesc_kmajor_noswz(sb + t0 * Cfg::B_PLANE, 128, 256),
+                 idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, Cfg::BM, np * BN), acc_in);
+        }
+      }
+      tc_commit(&empty_bar[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    tc_commit(accf_bar);
+  }
+}
 
 template <int BN, int KSMAX, int STAGES>
 __global__ void __launch_bounds__(192, 1)
@@ -109,14 +154,11 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* sb = sa + KSMAX * Cfg::A_PLANE;
         mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
         const int kc = p.k0 + kb * Cfg::BK;
-        for (int s = 0; s < ks; ++s) {
-          bulk_load(sa + s * Cfg::A_PLANE,
-                    p.dA + tiled_offset(static_cast<long long>(mb) * BM, kc, s, ks, p.rows_a_pad),
-                    Cfg::A_PLANE, &full_bar[stage]);
-          bulk_load(sb + s * Cfg::B_PLANE,
-                    p.dB + tiled_offset(static_cast<long long>(nb) * BN, kc, s, ks, p.rows_b_pad),
-                    Cfg::B_PLANE, &full_bar[stage]);
-        }
+        // all ks planes of each operand's row block: one contiguous chunk each
+        bulk_load(sa, p.dA + blocked_chunk(kc >> 5, mb, ks, p.rows_a_pad, 7),
+                  static_cast<uint32_t>(ks) * Cfg::A_PLANE, &full_bar[stage]);
+        bulk_load(sb, p.dB + blocked_chunk(kc >> 5, nb, ks, p.rows_b_pad, Cfg::BN_LOG2),
+                  static_cast<uint32_t>(ks) * Cfg::B_PLANE, &full_bar[stage]);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -140,39 +182,22 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    int stage = 0;
-    uint32_t phase = 0;
-    int it = 0;
-    bool aborted = false;
-    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x, ++it) {
-      if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) break;
-      tc_fence_after();
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-        const uint32_t sb = sa + KSMAX * Cfg::A_PLANE;
-        for (int s = 0; s < ks; ++s) {
-          const uint64_t ad = sdesc_kmajor_noswz(sa + s * Cfg::A_PLANE, 128, 256);
-          const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
-          for (int t0 = 0; t0 < ks - s; t0 += Cfg::PLANES_PER_MMA) {
-            const int np = min(Cfg::PLANES_PER_MMA, ks - s - t0);
-            const uint64_t bd = sdesc_kmajor_noswz(sb + t0 * Cfg::B_PLANE, 128, 256);
-            const uint32_t id = idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, BM, np * BN);
-            mma_i8(tmem_base + (s + t0) * BN, ad, bd, id, acc_in);
-          }
-        }
-        tc_commit(&empty_bar[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      if (aborted) break;
-      tc_commit(accf_bar);
+    // One fully unrolled issue loop per slice count: with compile-time plane
+    // offsets and shapes an MMA costs a few instructions to issue, where the
+    // runtime-ks loop spent more issue time than the tensor pipe spent on the
+    // (often narrow) MMAs themselves.
+    switch (ks) {
+#define TB_OZ_CASE(KS_)                                                        \
+  case KS_:                                                                    \
+    if constexpr (KS_ <= KSMAX && (KS_ > 8) == (BN == 32))                     \
+      oz_mma_role<BN, KSMAX, STAGES, KS_>(p, smem, full_bar, empty_bar, accf_bar, \
+                                          acce_bar, tmem_base, num_kb, ab);    \
+    break;
+      TB_OZ_CASE(1) TB_OZ_CASE(2) TB_OZ_CASE(3) TB_OZ_CASE(4) TB_OZ_CASE(5) TB_OZ_CASE(6)
+      TB_OZ_CASE(7) TB_OZ_CASE(8) TB_OZ_CASE(9) TB_OZ_CASE(10) TB_OZ_CASE(11) TB_OZ_CASE(12)
+#undef TB_OZ_CASE
+      default:
+        break;
     }
     tc_commit(drain_bar);
     const unsigned long long t0 = globaltimer_ns();
@@ -368,16 +393,18 @@ int trnblas_gemm_fp64(int64_t M, int64_t N, int64_t K, const double* A, int64_t 
   const long long ars = transA ? 1 : lda, aks = transA ? lda : 1;
   const long long brs = transB ? ldb : 1, bks = transB ? 1 : ldb;
   // one group of M (N) real rows padded to L.ma (L.nb): padding rows are zero
-  cudaError_t e = launch_split_tiled(A, ars, aks, static_cast<int>(M), static_cast<int>(K), M,
-                                     L.ma, L.ma, static_cast<int>(L.kp), slices, dA, eA, sc,
-                                     stream);
-  if (e == cudaSuccess)
-    e = launch_split_tiled(B, brs, bks, static_cast<int>(N), static_cast<int>(K), N, L.nb, L.nb,
-                           static_cast<int>(L.kp), slices, dB, eB, sc, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "ozaki split launch");
-
   const bool wide = slices <= 8;  // BN = 64 holds 8 diagonals; 9..12 use BN = 32
   const int BN = wide ? 64 : 32;
+  // A in row blocks of 128 (the MMA's M), B in row blocks of BN
+  cudaError_t e = launch_split_tiled(A, ars, aks, static_cast<int>(M), static_cast<int>(K), M,
+                                     L.ma, L.ma, static_cast<int>(L.kp), slices, dA, 7, nullptr,
+                                     0, eA, sc, stream);
+  if (e == cudaSuccess)
+    e = launch_split_tiled(B, brs, bks, static_cast<int>(N), static_cast<int>(K), N, L.nb, L.nb,
+                           static_cast<int>(L.kp), slices, dB, wide ? 6 : 5, nullptr, 0, eB, sc,
+                           stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ozaki split launch");
+
   OzParams p{};
   p.dA = dA;
   p.dB = dB;

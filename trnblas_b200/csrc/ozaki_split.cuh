@@ -134,31 +134,48 @@ __global__ void ozk_digits_kernel(const T* __restrict__ X, long long rs, long lo
   }
 }
 
-// Tiled digit layout: the image the int8 MMA reads from shared memory, so a
-// tile of any 8-aligned row range of one plane and one 32-wide K slab is one
-// contiguous chunk (fetched with a single bulk copy of whole 128-byte lines):
-//   [K slab (32)][plane][8-row group][K half (16)][row in group (8)][16 bytes]
-// i.e. no-swizzle K-major core matrices (8 rows x 16 bytes), LBO = 128 bytes
-// between the K halves, SBO = 256 bytes between row groups.
-__host__ __device__ __forceinline__ long long tiled_offset(long long p, int k, int s, int slices,
-                                                           long long rows_pad) {
+// Blocked digit layout: the image the int8 MMA reads from shared memory, laid
+// out so that all planes of one row block of one 32-wide K slab form a single
+// contiguous chunk, fetched with ONE bulk copy per operand and pipeline stage
+// (a bulk copy costs a fixed ~80 cycles of the SM's copy engine on top of its
+// bytes, so a stage staged as one copy per plane is copy-bound):
+//   [K slab (32)][row block (RB rows)][plane][8-row group][K half (16)]
+//   [row in group (8)][16 bytes]
+// Inside a chunk each plane is RB x 32 bytes of no-swizzle K-major core
+// matrices (8 rows x 16 bytes): LBO = 128 bytes between the K halves, SBO =
+// 256 bytes between row groups, planes RB * 32 bytes apart. RB = 2^rb_log2
+// (32, 64 or 128) is the MMA tile's row count for that operand.
+__host__ __device__ __forceinline__ long long blocked_offset(long long p, int k, int s, int slices,
+                                                             long long rows_pad, int rb_log2) {
   const long long slab = k >> 5;
   const int kk = k & 31;
-  return ((((slab * slices + s) * (rows_pad >> 3) + (p >> 3)) * 2 + (kk >> 4)) << 7) +
+  const long long nblk = rows_pad >> rb_log2;
+  const long long blk = p >> rb_log2;
+  const long long grp = (p & ((1ll << rb_log2) - 1)) >> 3;
+  return (((((((slab * nblk + blk) * slices + s) << (rb_log2 - 3)) + grp) * 2 + (kk >> 4))) << 7) +
          ((p & 7) << 4) + (kk & 15);
 }
 
-// Digits in the tiled layout. Padded row p maps to logical row
-// (p / gp) * g + p % gp when p % gp < g (else the row is zero padding): the
-// pair energy pads each occupied orbital's nvir rows to a multiple of 128, the
-// GEMM pads the end. 32 x 32 tiles; digits staged in shared memory, then
-// written 16 bytes at a time.
+// Start of the chunk of row block `blk` (all `slices` planes) of K slab `slab`.
+__host__ __device__ __forceinline__ long long blocked_chunk(long long slab, long long blk,
+                                                            int slices, long long rows_pad,
+                                                            int rb_log2) {
+  return ((slab * (rows_pad >> rb_log2) + blk) * slices) << (rb_log2 + 5);
+}
+
+// Digits in the blocked layout (row blocks of 2^rb_log2 rows), optionally a
+// second copy with another row block (digits2, rb_log2_2; NULL for none).
+// Padded row p maps to logical row (p / gp) * g + p % gp when p % gp < g (else
+// the row is zero padding): the pair energy pads each occupied orbital's nvir
+// rows to a multiple of 128, the GEMM pads the end. 32 x 32 tiles; digits
+// staged in shared memory, then written 16 bytes at a time.
 template <typename T>
 __global__ void ozk_digits_tiled_kernel(const T* __restrict__ X, long long rs, long long ks,
                                         int K, long long g, long long gp, long long rows_pad,
                                         int kpad, int slices, const int* __restrict__ exps,
                                         const int* __restrict__ shift_range,
-                                        int8_t* __restrict__ digits) {
+                                        int8_t* __restrict__ digits, int rb_log2,
+                                        int8_t* __restrict__ digits2, int rb_log2_2) {
   __shared__ double tile[32][33];
   __shared__ __align__(16) int8_t dg[12][32][32];
   const int k0 = blockIdx.x * 32;
@@ -208,21 +225,28 @@ __global__ void ozk_digits_tiled_kernel(const T* __restrict__ X, long long rs, l
   const int t = ty * 32 + tx;
   for (int it = t; it < slices * 64; it += 256) {
     const int s = it >> 6, row = (it >> 1) & 31, half = it & 1;
-    const long long off = tiled_offset(p0 + row, k0 + 16 * half, s, slices, rows_pad);
-    *reinterpret_cast<uint4*>(digits + off) = *reinterpret_cast<const uint4*>(&dg[s][row][16 * half]);
+    const uint4 v = *reinterpret_cast<const uint4*>(&dg[s][row][16 * half]);
+    *reinterpret_cast<uint4*>(digits + blocked_offset(p0 + row, k0 + 16 * half, s, slices,
+                                                      rows_pad, rb_log2)) = v;
+    if (digits2)
+      *reinterpret_cast<uint4*>(digits2 + blocked_offset(p0 + row, k0 + 16 * half, s, slices,
+                                                         rows_pad, rb_log2_2)) = v;
   }
 }
 
-// Split into the tiled layout: R logical rows (row r at X[r * rs + k * ks]),
-// rows_pad padded rows grouped as described above, K padded to kpad (multiple
-// of 32). scratch as for launch_split.
+// Split into the blocked layout: R logical rows (row r at X[r * rs + k * ks]),
+// rows_pad padded rows grouped as described above (a multiple of every row
+// block), K padded to kpad (multiple of 32); digits2 (may be NULL) receives a
+// second copy with row blocks of 2^rb_log2_2. scratch as for launch_split.
 template <typename T>
 inline cudaError_t launch_split_tiled(const T* X, long long rs, long long ks, int R, int K,
                                       long long g, long long gp, long long rows_pad, int kpad,
-                                      int slices, int8_t* digits, int* exps,
-                                      SplitScratch scratch, cudaStream_t stream) {
+                                      int slices, int8_t* digits, int rb_log2, int8_t* digits2,
+                                      int rb_log2_2, int* exps, SplitScratch scratch,
+                                      cudaStream_t stream) {
+  auto bad_rb = [&](int lg) { return lg < 5 || lg > 7 || (rows_pad & ((1ll << lg) - 1)); };
   if ((R + 31) / 32 > 65535 || rows_pad / 32 > 65535 || (rows_pad & 31) || (kpad & 31) ||
-      slices > 12)
+      slices > 12 || bad_rb(rb_log2) || (digits2 && bad_rb(rb_log2_2)))
     return cudaErrorInvalidConfiguration;
   ozk_init_kernel<<<(R + 255) / 256 + 1, 256, 0, stream>>>(scratch.maxbits, R,
                                                           scratch.shift_range);
@@ -233,7 +257,8 @@ inline cudaError_t launch_split_tiled(const T* X, long long rs, long long ks, in
                                                        scratch.shift_range);
   dim3 g3(static_cast<unsigned>(kpad / 32), static_cast<unsigned>(rows_pad / 32));
   ozk_digits_tiled_kernel<T><<<g3, blk, 0, stream>>>(X, rs, ks, K, g, gp, rows_pad, kpad, slices,
-                                                     exps, scratch.shift_range, digits);
+                                                     exps, scratch.shift_range, digits, rb_log2,
+                                                     digits2, rb_log2_2);
   return cudaGetLastError();
 }
 

@@ -43,7 +43,8 @@
 namespace tb {
 
 struct PairParams {
-  const int8_t* digits;    // tiled digit planes, rows (i, a) at i * nv_pad + a
+  const int8_t* digA;      // digits in 128-row blocks (A operand), rows (i, a) at i * nv_pad + a
+  const int8_t* digB;      // the same digits in 64-row blocks (B operand)
   long long rows_pad;      // nocc * nv_pad
   int nv_pad;              // nvir rounded up to 128 (zero rows beyond nvir)
   int nocc, nvir, naux_p;  // naux_p: K columns of the digit planes (multiple of 32)
@@ -155,16 +156,12 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-          const int kc = kb * Cfg::BK;
-#pragma unroll
-          for (int s = 0; s < KS; ++s) {
-            bulk_load(st + Cfg::A_OFF + s * Cfg::A_PLANE,
-                      p.digits + tiled_offset(ra, kc, s, KS, p.rows_pad), Cfg::A_PLANE,
-                      &full_bar[stage]);
-            bulk_load(st + Cfg::B_OFF + s * Cfg::B_PLANE,
-                      p.digits + tiled_offset(rb, kc, s, KS, p.rows_pad), Cfg::B_PLANE,
-                      &full_bar[stage]);
-          }
+          // all KS planes of the 128-row A block and of the 64-row B block:
+          // one contiguous chunk each
+          bulk_load(st + Cfg::A_OFF, p.digA + blocked_chunk(kb, ra >> 7, KS, p.rows_pad, 7),
+                    KS * Cfg::A_PLANE, &full_bar[stage]);
+          bulk_load(st + Cfg::B_OFF, p.digB + blocked_chunk(kb, rb >> 6, KS, p.rows_pad, 6),
+                    KS * Cfg::B_PLANE, &full_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -344,7 +341,7 @@ constexpr int kMaxGrid = 1024;
 
 struct PairLayout {
   long long naux_p, R, nv_pad, rows_pad;
-  size_t off_exps, off_max, off_range, off_part, total;
+  size_t off_digb, off_exps, off_max, off_range, off_part, total;
 };
 
 PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
@@ -353,8 +350,10 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
   L.R = nocc * nvir;
   L.nv_pad = round_up(std::max<long long>(nvir, 1), 128);
   L.rows_pad = nocc * L.nv_pad;
+  // the digits twice: in 128-row blocks (A operand) and in 64-row blocks (B)
   const size_t dig = static_cast<size_t>(round_up(kPairSlices * L.rows_pad * L.naux_p, 256));
-  L.off_exps = dig;
+  L.off_digb = dig;
+  L.off_exps = 2 * dig;
   L.off_max = L.off_exps + round_up(4 * L.R, 256);
   L.off_range = L.off_max + round_up(8 * L.R, 256);
   L.off_part = L.off_range + 256;
@@ -428,17 +427,19 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int8_t* dig = reinterpret_cast<int8_t*>(ws);
+  int8_t* digb = reinterpret_cast<int8_t*>(ws + L.off_digb);
   int* exps = reinterpret_cast<int*>(ws + L.off_exps);
   SplitScratch sc{reinterpret_cast<unsigned long long*>(ws + L.off_max),
                   reinterpret_cast<int*>(ws + L.off_range)};
   double* partials = reinterpret_cast<double*>(ws + L.off_part);
   cudaError_t e = launch_split_tiled(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
                                      nvir, L.nv_pad, L.rows_pad, static_cast<int>(L.naux_p),
-                                     kPairSlices, dig, exps, sc, stream);
+                                     kPairSlices, dig, 7, digb, 6, exps, sc, stream);
   if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
 
   PairParams p{};
-  p.digits = dig;
+  p.digA = dig;
+  p.digB = digb;
   p.rows_pad = L.rows_pad;
   p.nv_pad = static_cast<int>(L.nv_pad);
   p.nocc = static_cast<int>(nocc);

@@ -456,6 +456,13 @@ def check_slices(slices) -> int:
     return k
 
 
+def _all_finite(*xs: torch.Tensor) -> bool:
+    """True when no operand holds an Inf or NaN: one max-|x| reduction per
+    operand (NaN propagates through it) and a single host synchronisation."""
+    m = [torch.linalg.vector_norm(x, float("inf")) for x in xs if x.numel()]
+    return not m or bool(torch.isfinite(torch.stack(m)).all())
+
+
 def _gemm_fp64_device(a: torch.Tensor, b: torch.Tensor, k: int) -> torch.Tensor:
     """fp64 a @ b on the Ozaki int8 kernel (a, b finite fp64 on one CUDA device)."""
     M, K = a.shape
@@ -520,7 +527,7 @@ def gemm_fp64(
     b = _to(b.detach(), dev).to(torch.float64)
     if a.shape[1] == 0:
         r = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float64, device=dev)
-    elif not (bool(torch.isfinite(a).all()) and bool(torch.isfinite(b).all())):
+    elif not _all_finite(a, b):
         r = torch.matmul(a, b)
     else:
         r = _gemm_fp64_device(a, b, k)

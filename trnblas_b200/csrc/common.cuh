@@ -25,6 +25,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace tb {
 
 // ---------------------------------------------------------------------------
@@ -301,6 +303,23 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_noswz(uint32_t saddr, uint32_t 
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;  // sm_100 descriptor version; layout 0 = no swizzle
   return d;
+}
+
+// Calls f(std::integral_constant<int, I>{}) for I = 0 .. N-1, unrolled, so the
+// body sees I as a compile-time constant.
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (I < N) {
+    f(std::integral_constant<int, I>{});
+    static_for<I + 1, N>(f);
+  }
+}
+
+// A descriptor moved `bytes` further into shared memory (bytes a multiple of
+// 16). The start-address field holds addr >> 4 in 14 bits and shared-memory
+// addresses stay below 256 KB, so the add never carries out of the field.
+__host__ __device__ __forceinline__ constexpr uint64_t sdesc_add(uint64_t d, uint32_t bytes) {
+  return d + static_cast<uint64_t>(bytes >> 4);
 }
 
 // Generic K-major swizzled descriptor: layout 2 = 128B, 4 = 64B, 6 = 32B.

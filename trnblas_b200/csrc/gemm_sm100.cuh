@@ -77,6 +77,92 @@ struct GemmCfg {
   static_assert(KIND != kTF32x3 || BN == 128, "chunked epilogue keeps 128 columns in registers");
 };
 
+// MMA issuer role over this CTA's stream of K blocks (tiles x num_kb), chunked
+// into TMEM accumulator buffers as the epilogue expects (one chunk per tile
+// for kF16, CHUNK_KB K blocks for kTF32x3). The loop is unrolled over the
+// pipeline stages and the per-k-step descriptors are built once, so an MMA's
+// operands are a register plus a compile-time stage offset: a tcgen05.mma
+// issue holds the issuing thread until the tensor pipe is nearly ready for
+// it, and scalar work between the MMAs of consecutive stages (stage index
+// arithmetic, layout selects, descriptor rebuilds) shows up as idle tensor
+// cycles.
+template <int KIND, int BN, int STAGES>
+__device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem,
+                                              uint64_t* full_bar, uint64_t* empty_bar,
+                                              uint64_t* accf_bar, uint64_t* acce_bar,
+                                              uint32_t tmem_base, int num_kb, const Abort& ab) {
+  using Cfg = GemmCfg<KIND, BN>;
+  constexpr int SB = Cfg::STAGE_BYTES;
+  const uint32_t idesc_v = idesc(kAccF32, p.in_fmt, p.in_fmt, p.a_mn, p.b_mn, Cfg::BM, BN);
+  const uint32_t sa0 = smem_u32(smem);
+  const uint32_t sb0 = sa0 + Cfg::NPARTS * Cfg::A_TILE;
+  // k step kk of a stage: K-major operands advance 32 bytes inside the
+  // 128-byte swizzled row, MN-major (16-bit only) 16 K-rows = 2048 bytes
+  uint64_t ad[4], bd[4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    ad[kk] = (KIND == kF16 && p.a_mn) ? sdesc_sw128(sa0 + kk * 2048, 64 * 128, 1024)
+                                      : sdesc_sw128(sa0 + kk * 32, 16, 1024);
+    bd[kk] = (KIND == kF16 && p.b_mn) ? sdesc_sw128(sb0 + kk * 2048, 64 * 128, 1024)
+                                      : sdesc_sw128(sb0 + kk * 32, 16, 1024);
+  }
+  const int my_tiles =
+      p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const long long total = static_cast<long long>(my_tiles) * num_kb;
+  uint32_t phase = 0;
+  int gc = 0;   // accumulation chunks started
+  int kbt = 0;  // K block within the tile
+  int kbc = 0;  // K block within the chunk
+  uint32_t d_tmem = tmem_base;
+  bool stop = false;
+  for (long long g = 0; g < total && !stop; g += STAGES) {
+    static_for<0, STAGES>([&](auto sc) {
+      constexpr int S = decltype(sc)::value;
+      constexpr uint32_t OFF = static_cast<uint32_t>(S) * SB;
+      if (stop || g + S >= total) return;
+      if (kbc == 0) {
+        const int buf = gc % Cfg::NBUF;
+        const uint32_t bph = (gc / Cfg::NBUF) & 1;
+        if (!mbar_wait(&acce_bar[buf], bph ^ 1u, ab, kTimeoutAccEmpty)) {
+          stop = true;
+          return;
+        }
+        tc_fence_after();
+        d_tmem = tmem_base + buf * BN;
+      }
+      if (!mbar_wait(&full_bar[S], phase, ab, kTimeoutFull)) {
+        stop = true;
+        return;
+      }
+      tc_fence_after();
+      const bool first = kbc == 0;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t acc_in = (first && kk == 0) ? 0u : 1u;
+        if constexpr (KIND == kF16) {
+          mma_f16(d_tmem, sdesc_add(ad[kk], OFF), sdesc_add(bd[kk], OFF), idesc_v, acc_in);
+        } else {
+          const uint64_t ah = sdesc_add(ad[kk], OFF), al = sdesc_add(ad[kk], OFF + Cfg::A_TILE);
+          const uint64_t bh = sdesc_add(bd[kk], OFF), bl = sdesc_add(bd[kk], OFF + Cfg::B_TILE);
+          mma_tf32(d_tmem, al, bh, idesc_v, acc_in);  // small terms first
+          mma_tf32(d_tmem, ah, bl, idesc_v, 1u);
+          mma_tf32(d_tmem, ah, bh, idesc_v, 1u);
+        }
+      }
+      tc_commit(&empty_bar[S]);
+      ++kbt;
+      ++kbc;
+      if (kbc == Cfg::CHUNK_KB || kbt == num_kb) {
+        tc_commit(&accf_bar[gc % Cfg::NBUF]);
+        ++gc;
+        kbc = 0;
+        if (kbt == num_kb) kbt = 0;
+      }
+    });
+    phase ^= 1u;
+  }
+}
+
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz, int& mb,
                                             int& nb) {
   if (p.mode == kModeSyrk) {
@@ -336,60 +422,8 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc_v =
-        idesc(kAccF32, p.in_fmt, p.in_fmt, p.a_mn, p.b_mn, BM, BN);
-    int stage = 0;
-    uint32_t phase = 0;
-    int gc = 0;  // accumulation chunks issued by this CTA
-    bool aborted = false;
-    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x) {
-      for (int kb0 = 0; kb0 < num_kb && !aborted; kb0 += Cfg::CHUNK_KB, ++gc) {
-        const int buf = gc % Cfg::NBUF;
-        const uint32_t bph = (gc / Cfg::NBUF) & 1;
-        if (!mbar_wait(&acce_bar[buf], bph ^ 1u, ab, kTimeoutAccEmpty)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        const int kb_end = (num_kb - kb0 < Cfg::CHUNK_KB) ? num_kb : kb0 + Cfg::CHUNK_KB;
-        for (int kb = kb0; kb < kb_end; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) {
-            aborted = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t sb = sa + Cfg::NPARTS * Cfg::A_TILE;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc_in = (kb != kb0 || kk != 0) ? 1u : 0u;
-            if (KIND == kF16) {
-              const uint64_t ad = p.a_mn ? sdesc_sw128(sa + kk * 2048, 64 * 128, 1024)
-                                         : sdesc_sw128(sa + kk * 32, 16, 1024);
-              const uint64_t bd = p.b_mn ? sdesc_sw128(sb + kk * 2048, 64 * 128, 1024)
-                                         : sdesc_sw128(sb + kk * 32, 16, 1024);
-              mma_f16(d_tmem, ad, bd, idesc_v, acc_in);
-            } else {
-              const uint64_t ah = sdesc_sw128(sa + kk * 32, 16, 1024);
-              const uint64_t al = sdesc_sw128(sa + Cfg::A_TILE + kk * 32, 16, 1024);
-              const uint64_t bh = sdesc_sw128(sb + kk * 32, 16, 1024);
-              const uint64_t bl = sdesc_sw128(sb + Cfg::B_TILE + kk * 32, 16, 1024);
-              mma_tf32(d_tmem, al, bh, idesc_v, acc_in);  // small terms first
-              mma_tf32(d_tmem, ah, bl, idesc_v, 1u);
-              mma_tf32(d_tmem, ah, bh, idesc_v, 1u);
-            }
-          }
-          tc_commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (aborted) break;
-        tc_commit(&accf_bar[buf]);
-      }
-    }
+    gemm_mma_role<KIND, BN, STAGES>(p, smem, full_bar, empty_bar, accf_bar, acce_bar, tmem_base,
+                                    num_kb, ab);
     // Every MMA this thread issued must finish before TMEM is released.
     tc_commit(drain_bar);
     const unsigned long long t0 = globaltimer_ns();

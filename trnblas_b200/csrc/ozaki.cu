@@ -59,43 +59,69 @@ struct OzCfg {
 // MMA issuer role for exactly KS slices (compile time): every product of
 // diagonal d = s + t <= KS - 1 of each K slab, A-plane s against B-planes
 // t0 .. t0 + np - 1 stacked along N, into TMEM columns (s + t0) * BN.
-template <int BN, int KSMAX, int STAGES, int KS>
-__device__ __forceinline__ void oz_mma_role(const OzParams& p, uint8_t* smem, uint64_t* full_bar,
-                                            uint64_t* empty_bar, uint64_t* accf_bar,
-                                            uint64_t* acce_bar, uint32_t tmem_base, int num_kb,
-                                            const Abort& ab) {
+template <int BN, int KSMAX, int KS, int OFF>
+__device__ __forceinline__ void oz_issue(uint64_t dA, uint64_t dB, uint32_t tmem_base,
+                                         uint32_t acc) {
   using Cfg = OzCfg<BN, KSMAX>;
   constexpr int PPM = Cfg::PLANES_PER_MMA;
-  int stage = 0;
-  uint32_t phase = 0;
-  int it = 0;
-  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-    if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) return;
-    tc_fence_after();
-    for (int kb = 0; kb < num_kb; ++kb) {
-      if (!mbar_wait(&full_bar[stage], phase, ab, kTimeoutFull)) return;
-      tc_fence_after();
-      const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-      const uint32_t sb = sa + KSMAX * Cfg::A_PLANE;
 #pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const uint64_t ad = sdesc_kmajor_noswz(sa + s * Cfg::A_PLANE, 128, 256);
-        const uint32_t acc_in = (kb > 0 || s > 0) ? 1u : 0u;
+  for (int s = 0; s < KS; ++s) {
+    const uint64_t ad = sdesc_add(dA, OFF + s * Cfg::A_PLANE);
 #pragma unroll
-        for (int t0 = 0; t0 < KS - s; t0 += PPM) {
-          const int np = (KS - s - t0 < PPM) ? KS - s - t0 : PPM;
-          mma_i8(tmem_base + (s + t0) * BN, ad,
-                 sdesc_kmajor_noswz(sb + t0 * Cfg::B_PLANE, 128, 256),
-                 idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, Cfg::BM, np * BN), acc_in);
-        }
-      }
-      tc_commit(&empty_bar[stage]);
-      if (++stage == STAGES) {
-        stage = 0;
-        phase ^= 1u;
-      }
+    for (int t0 = 0; t0 < KS - s; t0 += PPM) {
+      const int np = (KS - s - t0 < PPM) ? KS - s - t0 : PPM;
+      mma_i8(tmem_base + (s + t0) * BN, ad, sdesc_add(dB, OFF + t0 * Cfg::B_PLANE),
+             idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, Cfg::BM, np * BN), (acc || s) ? 1u : 0u);
     }
-    tc_commit(accf_bar);
+  }
+}
+
+// MMA issuer role for exactly KS slices (compile time): every product of
+// diagonal d = s + t <= KS - 1 of each K slab, A-plane s against B-planes
+// t0 .. t0 + np - 1 stacked along N, into TMEM columns (s + t0) * BN. The
+// loop runs over this CTA's stream of `total` K slabs (tiles x num_kb) and is
+// unrolled over the pipeline stages, so every shared-memory offset and
+// barrier address is a compile-time constant: a tcgen05.mma issue holds the
+// issuing thread until the tensor pipe is nearly ready for it, so scalar work
+// between the MMAs of consecutive K slabs would leave the pipe idle.
+template <int BN, int KSMAX, int STAGES, int KS>
+__device__ __forceinline__ void oz_mma_role(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
+                                            uint64_t* accf_bar, uint64_t* acce_bar,
+                                            uint32_t tmem_base, int num_kb, long long total,
+                                            const Abort& ab) {
+  using Cfg = OzCfg<BN, KSMAX>;
+  const uint32_t base = smem_u32(smem);
+  const uint64_t dA = sdesc_kmajor_noswz(base, 128, 256);
+  const uint64_t dB = sdesc_kmajor_noswz(base + KSMAX * Cfg::A_PLANE, 128, 256);
+  uint32_t phase = 0;
+  int it = 0;   // tiles started
+  int kbt = 0;  // K slab within the current tile
+  bool stop = false;
+  for (long long g = 0; g < total && !stop; g += STAGES) {
+    static_for<0, STAGES>([&](auto sc) {
+      constexpr int S = decltype(sc)::value;
+      if (stop || g + S >= total) return;
+      if (kbt == 0) {
+        if (!mbar_wait(acce_bar, (it & 1) ^ 1u, ab, kTimeoutAccEmpty)) {
+          stop = true;
+          return;
+        }
+        tc_fence_after();
+      }
+      if (!mbar_wait(&full_bar[S], phase, ab, kTimeoutFull)) {
+        stop = true;
+        return;
+      }
+      tc_fence_after();
+      oz_issue<BN, KSMAX, KS, S * Cfg::STAGE_BYTES>(dA, dB, tmem_base, kbt > 0 ? 1u : 0u);
+      tc_commit(&empty_bar[S]);
+      if (++kbt == num_kb) {
+        kbt = 0;
+        ++it;
+        tc_commit(accf_bar);
+      }
+    });
+    phase ^= 1u;
   }
 }
 
@@ -186,12 +212,15 @@ __global__ void __launch_bounds__(192, 1)
     // offsets and shapes an MMA costs a few instructions to issue, where the
     // runtime-ks loop spent more issue time than the tensor pipe spent on the
     // (often narrow) MMAs themselves.
+    const long long my_tiles =
+        p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const long long total = my_tiles * num_kb;
     switch (ks) {
 #define TB_OZ_CASE(KS_)                                                        \
   case KS_:                                                                    \
     if constexpr (KS_ <= KSMAX && (KS_ > 8) == (BN == 32))                     \
-      oz_mma_role<BN, KSMAX, STAGES, KS_>(p, smem, full_bar, empty_bar, accf_bar, \
-                                          acce_bar, tmem_base, num_kb, ab);    \
+      oz_mma_role<BN, KSMAX, STAGES, KS_>(smem, full_bar, empty_bar, accf_bar,   \
+                                          acce_bar, tmem_base, num_kb, total, ab); \
     break;
       TB_OZ_CASE(1) TB_OZ_CASE(2) TB_OZ_CASE(3) TB_OZ_CASE(4) TB_OZ_CASE(5) TB_OZ_CASE(6)
       TB_OZ_CASE(7) TB_OZ_CASE(8) TB_OZ_CASE(9) TB_OZ_CASE(10) TB_OZ_CASE(11) TB_OZ_CASE(12)

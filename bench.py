@@ -7,7 +7,10 @@ value = whole-job TFLOP/s. The same line carries the DF-MP2 pair-energy step
 of config 5 (nocc 96, nvir 2208, naux 6912, pairs sharded over ranks) in ms.
 Other workloads (--workload): gemm_fp32 (config 5a fp32), gemm8192_bf16 /
 gemm8192_fp32 (single-GPU 8192^3), batched (config 2a), syrk (config 2b),
-gemm_fp64 (config 4), pair3 (config 3), pair5 (config 5b alone).
+gemm_fp64 (config 4), pair3 (config 3), pair5 (config 5b alone), pair5x4
+(config 5b per-pair shape at nocc 4, a small case for profiling), dfmp2 (the
+whole DF-MP2 energy, `parallel.df_mp2_energy`, at the reference's largest
+benchmark shape nbasis/nocc/naux = 768/96/2304).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
@@ -424,6 +427,11 @@ def run_pair(args, rank, world, gpu, nocc, nvir, naux, steps=None, warmup=None):
 # ── main ─────────────────────────────────────────────────────────────────────
 
 
+# nocc, nvir, naux: config 3, config 5b, and config 5b's per-pair shape at
+# nocc = 4 (a small case with the same units per pair, for profiling)
+PAIR_DIMS = {"pair3": (48, 432, 1152), "pair5": (96, 2208, 6912), "pair5x4": (4, 2208, 6912)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -432,7 +440,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="spmd",
                     choices=["spmd", "gemm_fp32", "gemm8192_bf16", "gemm8192_fp32", "pair3", "pair5",
-                             "gemm_fp64", "batched", "syrk"])
+                             "pair5x4", "dfmp2", "gemm_fp64", "batched", "syrk"])
     ap.add_argument("--no-pair", action="store_true", help="skip the pair-energy block of the default line")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -462,8 +470,10 @@ def run_ours(args, rank, world, gpu):
         if rank == 0:
             line["cpu_baseline"] = cpu_baseline_gemm(dt) if world == 1 else None
         return line
-    if args.workload in ("pair3", "pair5"):
-        dims = (48, 432, 1152) if args.workload == "pair3" else (96, 2208, 6912)
+    if args.workload == "dfmp2":
+        return run_dfmp2(args, rank, world, gpu)
+    if args.workload in PAIR_DIMS:
+        dims = PAIR_DIMS[args.workload]
         r = run_pair(args, rank, world, gpu, *dims)
         line = {
             "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
@@ -481,6 +491,109 @@ def run_ours(args, rank, world, gpu):
             line["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample}
         return line
     return run_single(args, rank, world, gpu)
+
+
+# nbasis, nocc, naux: the reference's largest DF-MP2 benchmark shape
+# ("large" in examples/df_mp2.py, docs/benchmarks.md "DF-MP2 end to end")
+DFMP2_DIMS = (768, 96, 2304)
+
+
+def run_dfmp2(args, rank, world, gpu):
+    """The whole DF-MP2 energy through `trnblas_b200.parallel.df_mp2_energy`
+    (metric factor, half transforms, metric contraction, pair energy; the
+    integral rows split over the ranks, strong scaling). value: ms per energy
+    with the inputs resident on every rank's GPU; e2e: the same call on
+    host inputs (each rank uploads its rows of the integrals)."""
+    from trnblas_b200 import _native as N
+    from trnblas_b200 import parallel as tp
+
+    nbasis, nocc, naux = DFMP2_DIMS
+    nvir = nbasis - nocc
+    g = torch.Generator(device="cuda").manual_seed(42)  # same inputs on every rank
+    C_occ = 0.1 * torch.randn(nbasis, nocc, device="cuda", generator=g)
+    C_vir = 0.1 * torch.randn(nbasis, nvir, device="cuda", generator=g)
+    eri = 0.01 * torch.randn(nbasis, nbasis, naux, device="cuda", generator=g)
+    R = 0.01 * torch.randn(naux, naux, device="cuda", generator=g)
+    J = R @ R.T + naux * torch.eye(naux, device="cuda")  # input construction, untimed
+    eo = -torch.sort(torch.rand(nocc, device="cuda", generator=g)).values - 0.5
+    ev = torch.sort(torch.rand(nvir, device="cuda", generator=g)).values + 0.1
+    ins = (C_occ, C_vir, eri, J, eo, ev)
+    out = {}
+
+    def step():
+        out["e"] = tp.df_mp2_energy(*ins)
+
+    N.launch_count = 0
+    steps, warmup = min(args.steps, 5), args.warmup
+    ms, clocks = timed_steps(step, steps, warmup, world, gpu)
+    launches = N.launch_count // (steps + warmup) * steps
+    t = {}
+    tp.df_mp2_energy(*ins, timings=t)
+    # e2e: host inputs, each rank uploads its rows of the integrals (pinned)
+    rows = tp._eri_rows(nbasis, world, False)[rank]
+    eri_h = torch.empty(eri.shape, dtype=eri.dtype, pin_memory=True)  # only this rank's rows are read
+    eri_h[rows[0]:rows[1]] = eri[rows[0]:rows[1]].cpu()
+    host = [x.cpu() for x in (C_occ, C_vir)] + [eri_h] + [x.cpu() for x in (J, eo, ev)]
+    del eri
+    torch.cuda.empty_cache()
+
+    def e2e_step():
+        out["e2e"] = tp.df_mp2_energy(*host)
+
+    e2e_ms, _ = timed_steps(e2e_step, max(2, steps // 2), 1, world, gpu)
+    h2d = (rows[1] - rows[0]) * nbasis * naux * 4 + sum(x.numel() * 4 for x in (C_occ, C_vir, J, eo, ev))
+    flops = (2.0 * nbasis * nbasis * nocc * naux + 2.0 * nocc * nvir * nbasis * naux
+             + 2.0 * nocc * nvir * naux * naux + nocc * (nocc + 1) / 2 * 2.0 * nvir * nvir * naux)
+    # dominant stage: the fused pair energy (int8 pipe), timed by the stage clock
+    nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
+    upp = sum(max(0, nC - 2 * r) for r in range(nR))
+    npairs_rank = (lambda pr: pr[1] - pr[0])(__import__("trnblas_b200").energy.pair_ranges(nocc, world)[rank])
+    int8_ops = npairs_rank * upp * 2 * (5 * 64 + 4 * 64 + 3 * 64 + 2 * 64 + 64) * 128 * math.ceil(naux / 32) * 32 * 2.0
+    pk, src = peaks()
+    e_ms = t.get("energy", float("nan")) * 1e3
+    ach = int8_ops / (e_ms / 1e3) / 1e12
+    line = {
+        "metric": f"DF-MP2 energy ms ({nbasis}/{nocc}/{naux}, end to end)",
+        "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 (3xTF32) GEMMs + int8 (5 Ozaki slices) pair energy",
+        "data": "synthetic (examples/df_mp2 distributions, device generator)",
+        "config": {"workload": "dfmp2", "nbasis": nbasis, "nocc": nocc, "naux": naux,
+                   "sharding": "integral rows by bytes, pairs by count"},
+        "energy": out["e"], "stage_seconds": {k: round(v, 5) for k, v in t.items()},
+        "tflops_fp32_equiv": round(flops / (ms / 1e3) / 1e12, 2),
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": 2.0 * pk["bf16_tflops"],
+                     "unit": "TOP/s (int8)", "frac": round(ach / (2.0 * pk["bf16_tflops"]), 4),
+                     "kernel": "pair_energy_kernel (energy stage)", "stage_ms": round(e_ms, 3),
+                     "traffic": None, "peak_source": f"{src}: 2 x bf16 burst (int8 dense rate)"},
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d * world),
+                "d2h_bytes_per_step": 8 * world, "path": "parallel.df_mp2_energy on host inputs"},
+        "clocks": clocks, "gpu_launches": launches,
+    }
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_dfmp2_sample(nbasis, nocc, naux)
+    return line
+
+
+def cpu_dfmp2_sample(nbasis, nocc, naux, budget_s: float = 10.0):
+    """The reference's CPU route for the whole DF-MP2 energy (torch fp32 on
+    the host): the energy stage from a pair sample (`cpu_pair_sample`), the
+    three GEMM stages from one timed sample GEMM scaled by flops."""
+    nvir = nbasis - nocc
+    e_ms, th, e_sample = cpu_pair_sample(nocc, nvir, naux, budget_s=budget_s)
+    g = torch.Generator().manual_seed(7)
+    cols = max(1, nbasis * naux // 16)
+    Ct = torch.randn(nocc, nbasis, generator=g)
+    E = torch.randn(nbasis, cols, generator=g)
+    Ct @ E
+    t0 = time.perf_counter()
+    Ct @ E
+    dt = time.perf_counter() - t0
+    rate = 2.0 * nocc * nbasis * cols / dt
+    gemm_flops = 2.0 * nbasis * nbasis * nocc * naux + 2.0 * nocc * nvir * nbasis * naux + 2.0 * nocc * nvir * naux * naux
+    total = e_ms + gemm_flops / rate * 1e3
+    return {"value": round(total, 1), "unit": "ms", "cores": th, "kind": "port",
+            "sample": f"{e_sample}; GEMM stages from a 1/16 half-transform sample at {rate / 1e12:.2f} TFLOP/s scaled by flops"}
 
 
 def cpu_baseline_gemm(dt):
@@ -595,8 +708,15 @@ def single_roofline(wl, A, B, flops):
 def reference_arm(args, world):
     """The reference's CPU route (restated in oracle/ and torch CPU), bounded sample."""
     torch.set_num_threads(os.cpu_count() or 1)
-    if args.workload in ("pair3", "pair5"):
-        dims = (48, 432, 1152) if args.workload == "pair3" else (96, 2208, 6912)
+    if args.workload == "dfmp2":
+        cb = cpu_dfmp2_sample(*DFMP2_DIMS, budget_s=8.0)
+        nb, no, na = DFMP2_DIMS
+        return {"impl": "reference", "metric": f"DF-MP2 energy ms ({nb}/{no}/{na}, end to end)",
+                "value": cb["value"], "unit": "ms", "higher_is_better": False, "n_gpus": world,
+                "steps": 1, "warmup": 1, "config": {"workload": "dfmp2"}, "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload in PAIR_DIMS:
+        dims = PAIR_DIMS[args.workload]
         ms, th, sample = cpu_pair_sample(*dims, budget_s=8.0)
         return {"impl": "reference", "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
                 "value": round(ms, 1), "unit": "ms", "higher_is_better": False, "n_gpus": world,

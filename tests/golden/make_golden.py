@@ -14,7 +14,12 @@ outputs of the hot-path functions:
   rows), trnblas.ozaki.reference_gemm, trnblas.gemm_fp64;
 - the pair energy: _torch_chunked_pair_energy (fp64 and fp32),
   _torch_batched_pair_energy, _pair_sym_reference, multicore.aten_rows row
-  ranges, on a small case and on config 3 (48/432/1152, seed 3).
+  ranges, on a small case and on config 3 (48/432/1152, seed 3);
+- DF-MP2 end to end (dfmp2.npz): examples/df_mp2.df_mp2_energy in fp32 and
+  fp64 on the example's own synthetic inputs, trnblas.parallel.df_mp2_energy
+  on one gloo rank (full and packed-symmetric integrals), trnblas.trsm over
+  side / uplo / trans / diag, trnblas.metric_inv_half.
+`--only dfmp2` writes just dfmp2.npz.
 Inputs that tests can regenerate from a seed are not stored when large.
 The torch / numpy versions used are written into meta.json.
 """
@@ -180,8 +185,58 @@ def energy_cases(dispatch, multicore, full: bool):
     return out
 
 
+def dfmp2_cases(trnblas):
+    """DF-MP2 pipeline and trsm outputs of the reference (CPU, torch route)."""
+    import os
+
+    import torch.distributed as dist
+
+    import examples.df_mp2 as ex  # the reference's example driver (PYTHONPATH)
+    from trnblas import parallel as rpar
+
+    out = {}
+    nbasis, nocc, naux, seed = 40, 6, 48, 11
+    C_occ, C_vir, eri, J, eo, ev = ex._make_inputs(nbasis, nocc, naux, seed=seed)
+    for k, v in dict(C_occ=C_occ, C_vir=C_vir, eri=eri, J=J, eo=eo, ev=ev).items():
+        out["in_" + k] = v.numpy()
+    out["E32"] = np.array(ex.df_mp2_energy(C_occ, C_vir, eri, J, eo, ev))
+    out["E64"] = np.array(ex.df_mp2_energy(*(x.double() for x in (C_occ, C_vir, eri, J, eo, ev))))
+    eri_s = 0.5 * (eri + eri.transpose(0, 1))
+    out["E64_sym"] = np.array(ex.df_mp2_energy(*(x.double() for x in (C_occ, C_vir, eri_s, J, eo, ev))))
+    out["X32"] = trnblas.metric_inv_half(J).numpy()
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        out["E32_par"] = np.array(rpar.df_mp2_energy(C_occ, C_vir, eri, J, eo, ev))
+        packed = rpar.pack_tril(eri_s)
+        out["E32_par_sym"] = np.array(rpar.df_mp2_energy(C_occ, C_vir, packed, J, eo, ev, eri_symmetric=True))
+        out["packed_sha"] = np.array(sha(packed))
+    finally:
+        dist.destroy_process_group()
+    g = torch.Generator().manual_seed(21)
+    n, m = 200, 24
+    # off-diagonal entries small enough that unit-diagonal solves stay
+    # well conditioned too
+    A = torch.randn(n, n, generator=g) / n + 2.0 * torch.eye(n)
+    B = torch.randn(n, m, generator=g)
+    out["trsm_A"], out["trsm_B"] = A.numpy(), B.numpy()
+    for side in ("left", "right"):
+        Bm = B if side == "left" else B.T.contiguous()
+        for uplo in ("upper", "lower"):
+            for trans in (False, True):
+                for diag in ("nonunit", "unit"):
+                    X = trnblas.trsm(0.5, A, Bm, side=side, uplo=uplo, trans=trans, diag=diag)
+                    out[f"trsm_{side}_{uplo}_{int(trans)}_{diag}"] = X.numpy()
+    return out
+
+
 def main():
     trnblas, ozaki, dispatch, multicore = _ref()
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "dfmp2":
+        np.savez_compressed(HERE / "dfmp2.npz", **dfmp2_cases(trnblas))
+        print("dfmp2.npz written")
+        return
     full = "--quick" not in sys.argv
     meta = {
         "reference": "trnsci/trnblas " + trnblas.__version__,

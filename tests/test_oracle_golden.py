@@ -236,3 +236,61 @@ def test_config3_inputs_and_energies_pinned():
     E64, E32 = float(z["cfg3_E64"]), float(z["cfg3_E32"])
     assert abs(E64 - (-237889.33113891596)) < 1e-6
     assert abs(E32 - E64) / abs(E64) < 1e-7  # the reference's own fp32 error
+
+
+# ── DF-MP2 end to end, trsm, metric factor ───────────────────────────────────
+
+
+def test_dfmp2_oracle_matches_reference_fp64():
+    from oracle import dfmp2
+
+    d = load("dfmp2.npz")
+    ins = [d["in_" + k] for k in ("C_occ", "C_vir", "eri", "J", "eo", "ev")]
+    e = dfmp2.df_mp2_energy(*ins)
+    assert abs(e - float(d["E64"])) <= 1e-11 * abs(float(d["E64"]))
+    # the reference's own fp32 pipeline and its SPMD driver agree to fp32 level
+    for k in ("E32", "E32_par"):
+        assert abs(float(d[k]) - e) <= 1e-5 * abs(e)
+
+
+def test_dfmp2_oracle_symmetric_packed():
+    from oracle import dfmp2
+
+    d = load("dfmp2.npz")
+    C_occ, C_vir, eri, J, eo, ev = (d["in_" + k] for k in ("C_occ", "C_vir", "eri", "J", "eo", "ev"))
+    eri_s = 0.5 * (eri + eri.transpose(1, 0, 2))
+    e = dfmp2.df_mp2_energy(C_occ, C_vir, eri_s, J, eo, ev)
+    assert abs(e - float(d["E64_sym"])) <= 1e-11 * abs(e)
+    assert abs(float(d["E32_par_sym"]) - e) <= 1e-5 * abs(e)
+    # pack_tril order: row mu (mu + 1) / 2 + nu, the reference's bytes
+    import torch as _t
+
+    from trnblas_b200.parallel import pack_tril
+
+    packed = pack_tril(_t.from_numpy(eri_s.astype(np.float32)))
+    assert hashlib.sha256(packed.contiguous().numpy().tobytes()).hexdigest() == str(d["packed_sha"])
+    assert np.array_equal(dfmp2.pack_tril(eri_s.astype(np.float32)), packed.numpy())
+
+
+def test_metric_inv_half_oracle_matches_reference():
+    from oracle import dfmp2
+
+    d = load("dfmp2.npz")
+    X = dfmp2.metric_inv_half(d["in_J"])
+    assert np.abs(X - d["X32"]).max() <= 1e-6 * np.abs(X).max()
+    assert np.allclose(X @ X.T, np.linalg.inv(d["in_J"].astype(np.float64)), rtol=1e-10, atol=1e-14)
+
+
+@pytest.mark.parametrize("side", ["left", "right"])
+@pytest.mark.parametrize("uplo", ["upper", "lower"])
+@pytest.mark.parametrize("trans", [False, True])
+@pytest.mark.parametrize("diag", ["nonunit", "unit"])
+def test_trsm_oracle_matches_reference(side, uplo, trans, diag):
+    from oracle import dfmp2
+
+    d = load("dfmp2.npz")
+    A, B = d["trsm_A"], d["trsm_B"]
+    Bm = B if side == "left" else B.T
+    X = dfmp2.trsm(0.5, A, Bm, side, uplo, trans, diag)
+    ref = d[f"trsm_{side}_{uplo}_{int(trans)}_{diag}"]
+    assert blas3.relf(ref, X) <= 1e-5

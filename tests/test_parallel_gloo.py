@@ -1,6 +1,8 @@
-"""SPMD host logic on 2 gloo CPU ranks (no GPU): the reference's GEMM
-primitives, the 2-D output-block GEMM and the pair-range energy split, with
-the local products replaced by CPU stand-ins (torch.matmul / the oracle)."""
+"""SPMD host logic on gloo CPU ranks (no GPU): the reference's GEMM
+primitives, the 2-D output-block GEMM, the pair-range energy split and the
+DF-MP2 pipeline (row split of the integrals, reduce-scatter, broadcast,
+all-gather), with the local products replaced by CPU stand-ins (torch.matmul
+in fp64 / the oracle)."""
 
 from __future__ import annotations
 
@@ -27,7 +29,11 @@ def _worker(rank, world, port, fn_name, q):
         import trnblas_b200.parallel as tp
         from oracle import pair_energy as PE
 
+        from oracle import dfmp2 as DF
+
         tp._local_mm = torch.matmul
+        tp._local_bmm = torch.matmul
+        tp._local_metric = lambda J: torch.from_numpy(DF.metric_inv_half(J.numpy())).float()
         tp._local_energy = lambda B, eo, ev, a, b: PE.pair_range_energy(B.numpy(), eo.numpy(), ev.numpy(), a, b)
         out = globals()[fn_name](rank, world, tp)
         q.put((rank, out))
@@ -44,7 +50,7 @@ def _run(fn_name, world=2):
     procs = [ctx.Process(target=_worker, args=(r, world, port, fn_name, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=120) for _ in procs)
+    res = dict(q.get(timeout=180) for _ in procs)
     for p in procs:
         p.join(timeout=60)
     return [res[r] for r in range(world)]
@@ -82,6 +88,65 @@ def _energy(rank, world, tp):
 
     B, eo, ev = PE.make_inputs(5, 9, 12, 3)
     return tp.pair_energy(B, eo, ev)
+
+
+def _dfmp2_inputs():
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "dfmp2.npz"))
+    return [torch.from_numpy(d["in_" + k]) for k in ("C_occ", "C_vir", "eri", "J", "eo", "ev")], d
+
+
+def _dfmp2(rank, world, tp):
+    ins, _ = _dfmp2_inputs()
+    t = {}
+    e = tp.df_mp2_energy(*ins, timings=t)
+    return [e, sorted(t)]
+
+
+def _dfmp2_sym(rank, world, tp):
+    (C_occ, C_vir, eri, J, eo, ev), _ = _dfmp2_inputs()
+    eri_s = 0.5 * (eri + eri.transpose(0, 1))
+    full = tp.df_mp2_energy(C_occ, C_vir, eri_s, J, eo, ev)
+    sym = tp.df_mp2_energy(C_occ, C_vir, eri_s, J, eo, ev, eri_symmetric=True)
+    packed = tp.df_mp2_energy(C_occ, C_vir, tp.pack_tril(eri_s), J, eo, ev, eri_symmetric=True)
+    return [full, sym, packed]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_df_mp2_energy_ranks_match_reference(world):
+    """nocc = 6 over 4 ranks pads the occupied rows; the fp32 inputs go
+    through fp32-rounded stand-ins, so the bar is fp32-level against the
+    reference's fp64 energy (its own fp32 pipeline is 1e-7 off)."""
+    _, d = _dfmp2_inputs()
+    ref = float(d["E64"])
+    outs = _run("_dfmp2", world)
+    for o in outs:
+        assert isinstance(o, list), o
+        assert abs(o[0] - ref) <= 1e-5 * abs(ref)
+        assert o[1] == sorted(["chol_upload_2a", "rs_iv_bcast_X", "local_2b_3", "ag_B", "energy"])
+    assert len({o[0] for o in outs}) == 1
+
+
+def test_df_mp2_energy_symmetric_and_packed_two_ranks():
+    _, d = _dfmp2_inputs()
+    ref = float(d["E64_sym"])
+    for o in _run("_dfmp2_sym", 2):
+        assert isinstance(o, list), o
+        for e in o:
+            assert abs(e - ref) <= 1e-5 * abs(ref)
+
+
+def test_eri_row_split_balances_bytes():
+    from trnblas_b200.parallel import _eri_rows
+
+    for n in (1, 7, 40, 301):
+        for parts in (1, 2, 3, 4, 8):
+            for sym in (False, True):
+                rows = _eri_rows(n, parts, sym)
+                assert len(rows) == parts and rows[0][0] == 0 and rows[-1][1] == n
+                assert all(a[1] == b[0] for a, b in zip(rows, rows[1:]))
+                if n >= 8 * parts:
+                    wt = [sum((mu + 1) if sym else 1 for mu in range(a, b)) for a, b in rows]
+                    assert max(wt) <= 1.5 * sum(wt) / parts + (n if sym else 1)
 
 
 def test_gemm_primitives_two_ranks():

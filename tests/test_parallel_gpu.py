@@ -1,7 +1,8 @@
 """SPMD paths on NCCL across the visible GPUs (one spawned process per GPU;
 skipped with fewer than 2 GPUs): the reference's GEMM primitives, the 2-D
-output-block GEMM, and the pair-range energy with its single fp64 all-reduce,
-each against the full single-process result."""
+output-block GEMM, the pair-range energy with its single fp64 all-reduce and
+the end-to-end DF-MP2 energy (full and packed-symmetric integrals), each
+against the full single-process result or the reference's fp64 energy."""
 
 from __future__ import annotations
 
@@ -66,6 +67,17 @@ def _worker(rank, world, port, q):
         ref = PE.chunked_energy(Bh.numpy(), eo.numpy(), ev.numpy())
         out["energy"] = abs(E - ref) <= 1e-9 * abs(ref)
         out["E"] = E
+        import numpy as np
+
+        d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "dfmp2.npz"))
+        ins = [torch.from_numpy(d["in_" + k]) for k in ("C_occ", "C_vir", "eri", "J", "eo", "ev")]
+        e_df = tp.df_mp2_energy(*ins)
+        out["dfmp2"] = abs(e_df - float(d["E64"])) <= 1e-5 * abs(float(d["E64"]))
+        C_occ, C_vir, eri, J, eo2, ev2 = ins
+        eri_s = 0.5 * (eri + eri.transpose(0, 1))
+        e_sym = tp.df_mp2_energy(C_occ, C_vir, tp.pack_tril(eri_s), J, eo2, ev2, eri_symmetric=True)
+        out["dfmp2_sym"] = abs(e_sym - float(d["E64_sym"])) <= 1e-5 * abs(float(d["E64_sym"]))
+        out["E_df"] = e_df
         out["status"] = tb.device_status(rank)
     except Exception as e:  # reported to the parent
         out["error"] = repr(e)
@@ -94,3 +106,4 @@ def test_spmd_on_nccl():
         assert not bad, (r, bad)
         assert res[r]["status"] == 0
     assert len({res[r]["E"] for r in range(world)}) == 1
+    assert len({res[r]["E_df"] for r in range(world)}) == 1

@@ -35,6 +35,7 @@
 // the same block, X(2X-Y) / D once; a in block 2R+1 with b in block 2R is
 // skipped (unit (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
 #include <algorithm>
+#include <cmath>
 #include <string>
 
 #include "ozaki_split.cuh"
@@ -49,6 +50,7 @@ struct PairParams {
   int nv_pad;              // nvir rounded up to 128 (zero rows beyond nvir)
   int nocc, nvir, naux_p;  // naux_p: K columns of the digit planes (multiple of 32)
   long long pair_begin;
+  const int2* order;       // (i, j) of the range's pairs in processing order
   long long num_units;     // pairs * units_per_pair
   int units_per_pair;
   int nR, nC;              // 128-blocks and 64-blocks of nvir
@@ -78,11 +80,41 @@ __device__ __forceinline__ void pair_of(long long p, int& i, int& j) {
   i = static_cast<int>(p - jj * (jj + 1) / 2);
 }
 
+// Pairs of [begin, end) (linear index tri(j) + i, i <= j) in an L2-friendly
+// order: rows j in chunks of g, and inside a chunk the pairs grouped by
+// g-wide blocks of i, so that consecutive units (which run at the same time on
+// different SMs) share the digits of at most 2g occupied orbitals. One thread
+// per chunk; a chunk's pairs are contiguous in the linear order, so its first
+// output position is known in closed form.
+__global__ void pair_order_kernel(long long begin, long long end, int g, int2* __restrict__ order) {
+  int i0, j0, i1, j1;
+  pair_of(begin, i0, j0);
+  pair_of(end - 1, i1, j1);
+  const long long c = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long rs = j0 + c * g;
+  if (rs > j1) return;
+  const long long re = (rs + g < j1 + 1) ? rs + g : j1 + 1;
+  const long long first = rs * (rs + 1) / 2;
+  long long pos = first > begin ? first - begin : 0;
+  for (long long ib = 0; ib * g < re; ++ib) {
+    for (long long r = rs; r < re; ++r) {
+      const long long ihi = (ib * g + g < r + 1) ? ib * g + g : r + 1;
+      for (long long i = ib * g; i < ihi; ++i) {
+        const long long q = r * (r + 1) / 2 + i;
+        if (q < begin || q >= end) continue;
+        order[pos++] = make_int2(static_cast<int>(i), static_cast<int>(r));
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void unit_of(const PairParams& p, long long u, int& i, int& j, int& R,
                                         int& C) {
   const long long pr = u / p.units_per_pair;
   int loc = static_cast<int>(u - pr * p.units_per_pair);
-  pair_of(p.pair_begin + pr, i, j);
+  const int2 ij = p.order[pr];
+  i = ij.x;
+  j = ij.y;
   R = 0;
   while (R < p.nR) {
     const int cnt = p.nC - 2 * R;
@@ -372,10 +404,10 @@ constexpr int kMaxGrid = 1024;
 
 struct PairLayout {
   long long naux_p, R, nv_pad, rows_pad;
-  size_t off_digb, off_exps, off_max, off_range, off_part, total;
+  size_t off_digb, off_exps, off_max, off_range, off_part, off_order, total;
 };
 
-PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
+PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long npairs) {
   PairLayout L{};
   L.naux_p = round_up(std::max<long long>(naux, 1), 32);
   L.R = nocc * nvir;
@@ -388,8 +420,28 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux) {
   L.off_max = L.off_exps + round_up(4 * L.R, 256);
   L.off_range = L.off_max + round_up(8 * L.R, 256);
   L.off_part = L.off_range + 256;
-  L.total = L.off_part + round_up(8 * kMaxGrid, 256);
+  L.off_order = L.off_part + round_up(8 * kMaxGrid, 256);
+  L.total = L.off_order + round_up(8 * std::max<long long>(npairs, 1), 256);
   return L;
+}
+
+// Pair-block width g of the processing order: the digits of 2g occupied
+// orbitals (both layouts) should fit in half of L2.
+int pair_block(const PairLayout& L, long long nocc) {
+  int l2 = 0;
+  if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, current_device()) != cudaSuccess || l2 <= 0)
+    l2 = 96 << 20;
+  const double per_orb = 2.0 * kPairSlices * static_cast<double>(L.nv_pad) * L.naux_p;
+  const long long g = static_cast<long long>(0.5 * l2 / (2.0 * per_orb));
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(g, std::max<long long>(nocc, 1))));
+}
+
+void host_pair_of(long long p, int& i, int& j) {
+  long long jj = static_cast<long long>((std::sqrt(8.0 * static_cast<double>(p) + 1.0) - 1.0) * 0.5);
+  while (jj * (jj + 1) / 2 > p) --jj;
+  while ((jj + 1) * (jj + 2) / 2 <= p) ++jj;
+  j = static_cast<int>(jj);
+  i = static_cast<int>(p - jj * (jj + 1) / 2);
 }
 
 int units_per_pair(long long nvir) {
@@ -408,10 +460,8 @@ extern "C" {
 
 size_t trnblas_pair_energy_workspace_size(int64_t nocc, int64_t nvir, int64_t naux,
                                           int64_t pair_begin, int64_t pair_end) {
-  (void)pair_begin;
-  (void)pair_end;
   if (nocc <= 0 || nvir <= 0 || naux <= 0) return 256;
-  return pair_layout(nocc, nvir, naux).total;
+  return pair_layout(nocc, nvir, naux, std::max<int64_t>(pair_end - pair_begin, 0)).total;
 }
 
 int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B,
@@ -451,7 +501,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   const long long num_units = (pair_end - pair_begin) * static_cast<long long>(upp);
   const int grid = static_cast<int>(
       std::min<long long>(std::min<long long>(num_units, num_sms()), kMaxGrid));
-  const PairLayout L = pair_layout(nocc, nvir, naux);
+  const PairLayout L = pair_layout(nocc, nvir, naux, pair_end - pair_begin);
   if (!workspace || workspace_bytes < L.total) {
     set_error("trnblas_pair_energy needs " + std::to_string(L.total) + " workspace bytes");
     return TRNBLAS_ERR_WORKSPACE;
@@ -463,10 +513,20 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   SplitScratch sc{reinterpret_cast<unsigned long long*>(ws + L.off_max),
                   reinterpret_cast<int*>(ws + L.off_range)};
   double* partials = reinterpret_cast<double*>(ws + L.off_part);
+  int2* order = reinterpret_cast<int2*>(ws + L.off_order);
   cudaError_t e = launch_split_tiled(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
                                      nvir, L.nv_pad, L.rows_pad, static_cast<int>(L.naux_p),
                                      kPairSlices, dig, 7, digb, 6, exps, sc, stream);
   if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
+  {
+    const int g = pair_block(L, nocc);
+    int i0, j0, i1, j1;
+    host_pair_of(pair_begin, i0, j0);
+    host_pair_of(pair_end - 1, i1, j1);
+    const long long chunks = (j1 - j0) / g + 1;
+    pair_order_kernel<<<static_cast<unsigned>((chunks + 127) / 128), 128, 0, stream>>>(
+        pair_begin, pair_end, g, order);
+  }
 
   PairParams p{};
   p.digA = dig;
@@ -477,6 +537,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   p.nvir = static_cast<int>(nvir);
   p.naux_p = static_cast<int>(L.naux_p);
   p.pair_begin = pair_begin;
+  p.order = order;
   p.num_units = num_units;
   p.units_per_pair = upp;
   p.nR = static_cast<int>(ceil_div(nvir, 128));

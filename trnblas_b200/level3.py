@@ -1,4 +1,5 @@
-"""BLAS level 3 on B200: gemm, batched_gemm, syrk, gemm_fp64.
+"""BLAS level 3 on B200: gemm, batched_gemm, syrk, gemm_fp64, trsm,
+metric_inv_half.
 
 Same signatures, argument meanings, return dtypes and exceptions as the
 reference's trnblas/level3.py (gemm :69-109, batched_gemm :112-134, gemm_fp64
@@ -20,7 +21,7 @@ import warnings
 import torch
 
 from . import _native as N
-from ._flags import trans_flag, uplo_flag
+from ._flags import diag_flag, side_flag, trans_flag, uplo_flag
 
 # ── device placement ─────────────────────────────────────────────────────────
 
@@ -532,3 +533,124 @@ def gemm_fp64(
     else:
         r = _gemm_fp64_device(a, b, k)
     return r.to(home) if home != dev else r
+
+
+# ── triangular solve and the density-fitting metric factor ──────────────────
+
+# Rows of one diagonal panel of the blocked solve. Panels solve with
+# torch.linalg.solve_triangular (small, sequential); everything else is
+# trailing-update GEMMs on the tcgen05 kernel, so larger panels shift work
+# from the sequential solves to the GEMM.
+TRSM_PANEL = 256
+
+
+def _trsm_torch(alpha, A, B, side, uplo, trans, diag):
+    """op(A) X = alpha B (left) / X op(A) = alpha B (right) with torch, for
+    dtypes that have no kernel (as the reference's host route does,
+    trnblas/nki/dispatch.py:1707-1738)."""
+    tri = torch.triu(A) if uplo == "upper" else torch.tril(A)
+    mat = tri.mT if trans else tri
+    upper = (uplo == "upper") != trans
+    X = torch.linalg.solve_triangular(mat, B, upper=upper, left=side == "left", unitriangular=diag == "unit")
+    return alpha * X
+
+
+def _trsm_left_blocked(alpha: float, A: torch.Tensor, B: torch.Tensor, uplo: str, trans: bool, unit: bool):
+    """op(A) X = alpha B on the GPU in fp32: diagonal panels by
+    solve_triangular, trailing updates X_rest -= op(A)_rest,panel X_panel by
+    the 3xTF32 GEMM (beta = 1 fused). Forward substitution when op(A) is lower
+    triangular, backward when upper. Reads only op(A)'s triangle (and not its
+    diagonal for a unit diagonal)."""
+    mat = A.mT if trans else A
+    lower = (uplo == "lower") != trans
+    n = mat.shape[0]
+    X = (B * alpha) if alpha != 1.0 else B.clone()
+    P = TRSM_PANEL
+    if n <= P:
+        return torch.linalg.solve_triangular(mat, X, upper=not lower, unitriangular=unit)
+    if lower:
+        for k0 in range(0, n, P):
+            k1 = min(k0 + P, n)
+            X[k0:k1] = torch.linalg.solve_triangular(mat[k0:k1, k0:k1], X[k0:k1], upper=False, unitriangular=unit)
+            if k1 < n:
+                X[k1:] = _gemm_public(-1.0, mat[k1:, k0:k1], X[k0:k1], 1.0, X[k1:])
+    else:
+        for k1 in range(n, 0, -P):
+            k0 = max(k1 - P, 0)
+            X[k0:k1] = torch.linalg.solve_triangular(mat[k0:k1, k0:k1], X[k0:k1], upper=True, unitriangular=unit)
+            if k0 > 0:
+                X[:k0] = _gemm_public(-1.0, mat[:k0, k0:k1], X[k0:k1], 1.0, X[:k0])
+    return X
+
+
+def trsm(
+    alpha: float,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    side: str = "left",
+    uplo: str = "upper",
+    trans: bool = False,
+    diag: str = "nonunit",
+) -> torch.Tensor:
+    """Triangular solve with multiple right-hand sides (trnblas/level3.py:332-362):
+    op(A) @ X = alpha * B (side 'left') or X @ op(A) = alpha * B ('right');
+    returns X. Only the `uplo` triangle of A is read; diag 'unit' takes its
+    diagonal as ones.
+
+    float32 / bfloat16 / float16 solve blocked on the GPU in fp32 (the
+    trailing updates are the 3xTF32 GEMM kernel, the diagonal panels
+    solve_triangular) and return B's dtype on B's device; a right-side solve
+    is the left solve of the transposed system. Other dtypes run torch, as in
+    the reference.
+    """
+    side, uplo, diag = side_flag(side), uplo_flag(uplo), diag_flag(diag)
+    trans = trans_flag(trans)
+    if A.dim() != 2 or A.shape[0] != A.shape[1]:
+        raise ValueError(f"trsm: A must be a square matrix, got {tuple(A.shape)}")
+    if A.dtype not in N.KERNEL_DTYPES or B.dtype not in N.KERNEL_DTYPES:
+        return _trsm_torch(alpha, A, B, side, uplo, trans, diag)
+    vec = B.dim() == 1
+    b = B.unsqueeze(1 if side == "left" else 0) if vec else B
+    if b.dim() != 2:
+        raise ValueError(f"trsm: B must be 1-D or 2-D, got {tuple(B.shape)}")
+    n = A.shape[0]
+    if (side == "left" and b.shape[0] != n) or (side == "right" and b.shape[1] != n):
+        raise ValueError(f"trsm: A is {n}x{n} but B is {tuple(B.shape)} for side={side!r}")
+    home = B.device
+    dev = _cuda_device(A, B)
+    a32 = _to(A, dev).to(torch.float32)
+    b32 = _to(b, dev).to(torch.float32)
+    if side == "left":
+        X = _trsm_left_blocked(alpha, a32, b32, uplo, trans, diag == "unit")
+    else:  # X op(A) = alpha B  <=>  op(A)^T X^T = alpha B^T
+        X = _trsm_left_blocked(alpha, a32, b32.mT.contiguous(), uplo, not trans, diag == "unit").mT.contiguous()
+    if vec:
+        X = X.reshape(-1)
+    X = X.to(B.dtype)
+    return X.to(home) if home != dev else X
+
+
+def metric_inv_half(J: torch.Tensor) -> torch.Tensor:
+    """Cholesky inverse factor of a symmetric positive definite metric,
+    X = L^-T with J = L L^T (trnblas/level3.py:365-380), so X X^T = J^-1 and
+    (ia|Q) @ X is the density-fitting metric contraction of DF-MP2.
+
+    Cholesky with torch.linalg.cholesky (cuSOLVER), then the blocked trsm
+    (L^T X = I) on the GPU; float32 / bfloat16 / float16 compute in fp32.
+    Returns J's dtype on J's device. Other float dtypes run torch; integer
+    input raises NotImplementedError, as in the reference.
+    """
+    if not (J.is_floating_point() or J.is_complex()):
+        raise NotImplementedError(f"metric_inv_half: expected a floating point or complex tensor; got {J.dtype}")
+    if J.dim() != 2 or J.shape[0] != J.shape[1]:
+        raise ValueError(f"metric_inv_half: J must be a square matrix, got {tuple(J.shape)}")
+    if J.dtype not in N.KERNEL_DTYPES:
+        L = torch.linalg.cholesky(J)
+        eye = torch.eye(J.shape[0], dtype=J.dtype, device=J.device)
+        return _trsm_torch(1.0, L, eye, "left", "lower", True, "nonunit")
+    home = J.device
+    dev = _cuda_device(J)
+    L = torch.linalg.cholesky(_to(J, dev).to(torch.float32))
+    eye = torch.eye(J.shape[0], dtype=torch.float32, device=dev)
+    X = trsm(1.0, L, eye, uplo="lower", trans=True).to(J.dtype)
+    return X.to(home) if home != dev else X

@@ -18,6 +18,11 @@ Additions for B200:
   overlaps the gather of chunk k+1. `shard_2d` slices full operands.
 - `pair_energy` shards the linearised i <= j pair list by pair count (every
   pair costs the same) and sums one fp64 scalar with a single all-reduce.
+- `df_mp2_energy` is the whole DF-MP2 energy from MO coefficients, 3-centre
+  integrals and the metric (trnblas/parallel.py:258-353): every rank uploads
+  its rows of the integrals and half-transforms them, a reduce-scatter sums
+  the partials over occupied rows, the metric factor is broadcast, each rank
+  forms its rows of B, B is all-gathered and the pair energy split as above.
 The routines also run on gloo with CPU tensors when the local products are
 given a CPU implementation (`_local_mm`, `_local_energy`), which is how they
 are unit-tested.
@@ -30,11 +35,17 @@ import math
 import torch
 import torch.distributed as dist
 
+import time
+
 from . import energy as _energy
+from .level3 import batched_gemm as _batched_gemm
 from .level3 import gemm as _gemm
+from .level3 import metric_inv_half as _metric_inv_half
 
 # Local products: the B200 kernels. CPU/gloo tests replace them.
 _local_mm = None
+_local_bmm = None
+_local_metric = None
 _local_energy = None
 
 
@@ -42,6 +53,12 @@ def _mm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     if _local_mm is not None:
         return _local_mm(a, b)
     return _gemm(1.0, a, b)
+
+
+def _bmm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    if _local_bmm is not None:
+        return _local_bmm(a, b)
+    return _batched_gemm(1.0, a, b)
 
 
 def device() -> torch.device:
@@ -53,6 +70,10 @@ def device() -> torch.device:
 
 def _rank_world(group) -> tuple[int, int]:
     return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _distributed() -> bool:
+    return dist.is_available() and dist.is_initialized()
 
 
 def _reduce_scatter(out: torch.Tensor, inp: torch.Tensor, group) -> None:
@@ -263,26 +284,205 @@ def pair_energy(
     relative accuracy would not survive an fp32 sum). Returns a float on
     every rank.
     """
-    r, w = _rank_world(group)
+    r, w = _rank_world(group) if _distributed() else (0, 1)
     nocc = B_full.shape[0]
     p0, p1 = _energy.pair_ranges(nocc, w)[r]
     if _local_energy is not None:
         e = torch.as_tensor(_local_energy(B_full, eps_occ, eps_vir, p0, p1), dtype=torch.float64).reshape(1)
     else:
         e = _energy.pair_range_energy(B_full, eps_occ, eps_vir, p0, p1).reshape(1)
-    dist.all_reduce(e, group=group)
+    if w > 1:
+        dist.all_reduce(e, group=group)
     return float(e.cpu())
+
+
+# ── DF-MP2 energy end to end ─────────────────────────────────────────────────
+
+
+def pack_tril(eri_3c: torch.Tensor) -> torch.Tensor:
+    """(nbasis, nbasis, naux) integrals symmetric in the first two indices ->
+    their packed lower triangle (npair, naux), pair (mu, nu <= mu) at row
+    mu (mu + 1) / 2 + nu (PySCF's pack_tril order; its `_cderi` is this
+    transposed), as trnblas/parallel.py:188-197."""
+    n = eri_3c.shape[0]
+    r, c = torch.tril_indices(n, n, device=eri_3c.device)
+    return eri_3c[r, c]
+
+
+def _eri_rows(nbasis: int, parts: int, symmetric: bool) -> list[tuple[int, int]]:
+    """`parts` contiguous ranges of mu balanced by the bytes each uploads: a
+    full row weighs nbasis, a packed lower-triangle row mu + 1."""
+    weights = [mu + 1 if symmetric else 1 for mu in range(nbasis)]
+    total = sum(weights)
+    bounds, acc, start = [], 0, 0
+    for mu, wt in enumerate(weights):
+        acc += wt
+        if len(bounds) < parts - 1 and acc * parts >= total * (len(bounds) + 1):
+            bounds.append((start, mu + 1))
+            start = mu + 1
+    bounds.append((start, nbasis))
+    while len(bounds) < parts:
+        bounds.append((nbasis, nbasis))
+    return bounds
+
+
+def _rows_lower_triangle(eri_3c: torch.Tensor, m0: int, m1: int, nbasis: int, dev) -> torch.Tensor:
+    """Rows mu in [m0, m1) as (n_r, nbasis, naux) on `dev` with (mu nu|P) for
+    nu <= mu and zeros above the diagonal, uploading only the lower triangle
+    (`eri_3c` full (nbasis, nbasis, naux) or packed (npair, naux))."""
+    p0, p1 = m0 * (m0 + 1) // 2, m1 * (m1 + 1) // 2
+    if eri_3c.dim() == 2:
+        packed = eri_3c[p0:p1]
+    else:
+        packed = torch.cat([eri_3c[mu, : mu + 1] for mu in range(m0, m1)])
+    naux = packed.shape[-1]
+    buf = torch.zeros((p1 - p0 + 1, naux), dtype=torch.float32, device=dev)  # last row stays zero
+    buf[: p1 - p0].copy_(packed)
+    mu = torch.arange(m0, m1, device=dev)
+    nu = torch.arange(nbasis, device=dev)
+    src = (mu * (mu + 1) // 2 - p0)[:, None] + nu[None, :]
+    src = torch.where(nu[None, :] <= mu[:, None], src, torch.full_like(src, p1 - p0))
+    return buf.index_select(0, src.reshape(-1)).reshape(m1 - m0, nbasis, naux)
+
+
+def _half_transform_part(Cp: torch.Tensor, eri_3c: torch.Tensor, rows, dev, symmetric: bool, nbasis: int):
+    """This rank's share of (i nu|P) = sum_mu C[mu, i] (mu nu|P), summed over
+    its rows mu of the integrals: (nocc_pad, nbasis * naux) on `dev`.
+
+    With `symmetric`, (mu nu|P) = (nu mu|P) and only the lower triangle of
+    the rows is uploaded; the mirrored entries (nu < mu) contribute through the
+    same data: sum_{nu < mu} C[nu, i] (mu nu|P) is added to (i mu|P)."""
+    naux = eri_3c.shape[-1]
+    m0, m1 = rows
+    n_r = m1 - m0
+    nocc_pad = Cp.shape[1]
+    if n_r == 0:
+        return torch.zeros((nocc_pad, nbasis * naux), dtype=torch.float32, device=dev)
+    Cr = Cp[m0:m1].to(dev)  # (n_r, nocc_pad)
+    if not symmetric:
+        eri_r = eri_3c[m0:m1].reshape(n_r, nbasis * naux).to(dev, torch.float32)
+        return _mm(Cr.T, eri_r)
+    L = _rows_lower_triangle(eri_3c, m0, m1, nbasis, dev)  # (n_r, nbasis, naux)
+    part = _mm(Cr.T, L.reshape(n_r, nbasis * naux))  # the nu <= mu terms
+    # mirrored terms for every mu of the range: C^T (nocc_pad, nbasis) @ L[mu]
+    # counts nu <= mu; the diagonal nu == mu is already in `part`
+    CT = Cp.T.contiguous().to(dev)
+    Mr = _bmm(CT.unsqueeze(0).expand(n_r, nocc_pad, nbasis), L)  # (n_r, nocc_pad, naux)
+    diag = L[torch.arange(n_r, device=dev), torch.arange(m0, m1, device=dev)]  # (n_r, naux)
+    Mr = Mr - Cr.unsqueeze(2) * diag.unsqueeze(1)
+    part.view(nocc_pad, nbasis, naux)[:, m0:m1, :] += Mr.permute(1, 0, 2)
+    return part
+
+
+def df_mp2_energy(
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    eri_3c: torch.Tensor,
+    J_metric: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    group=None,
+    timings: dict | None = None,
+    eri_symmetric: bool = False,
+) -> float:
+    """DF-MP2 correlation energy, split over the ranks of `group`
+    (trnblas/parallel.py:258-353; examples/df_mp2.py:147-228 on one GPU).
+
+    C_occ (nbasis, nocc), C_vir (nbasis, nvir), eri_3c (nbasis, nbasis,
+    naux) three-centre integrals (mu nu|P), J_metric (naux, naux) SPD, the
+    orbital energies; host or device tensors, the same on every rank (each
+    rank reads only its rows of eri_3c). `eri_symmetric=True` declares
+    (mu nu|P) = (nu mu|P): only lower triangles are read and uploaded, and
+    eri_3c may then be the packed (npair, naux) triangle of `pack_tril`.
+    Without an initialised process group it runs on this process's GPU.
+    Returns the energy (a float) on every rank; `timings` receives seconds
+    per stage under the reference's keys.
+
+    Dataflow (r = rank, w = world size):
+    1+2a. rank 0 forms X = J^-1/2 (`metric_inv_half`, Cholesky + blocked
+          trsm); every rank uploads its byte-balanced rows mu_r of the
+          integrals and forms its partial (i nu|P) = C_occ[mu_r]^T (mu_r nu|P)
+          on the GEMM kernel (each GPU has its own host link, so unlike the
+          reference no rank is kept off the upload);
+    2b.   a reduce-scatter over occupied rows (padded to a multiple of w)
+          leaves rank r its occ_r rows of (i nu|P); X is broadcast;
+    3.    (ia|P) = C_vir^T (i nu|P) (batched GEMM, C_vir^T broadcast) and
+          B = (ia|P) X for those rows;
+    4.    B is all-gathered and the fused pair-energy kernel sums the rank's
+          pair range; one fp64 all-reduce.
+    All products are fp32 on the tensor cores (3xTF32), as the reference's
+    fp32 pipeline.
+    """
+    if eri_3c.dim() == 2 and not eri_symmetric:
+        raise ValueError("a packed (npair, naux) eri_3c needs eri_symmetric=True")
+    multi = _distributed()
+    r, w = _rank_world(group) if multi else (0, 1)
+    dev = device()
+    nbasis, nocc = C_occ.shape
+    nvir = C_vir.shape[1]
+    naux = J_metric.shape[0]
+    occ_r = -(-nocc // w)
+    nocc_pad = occ_r * w
+    t = {}
+    clock = [time.perf_counter()]
+
+    def mark(name):
+        if timings is not None:
+            if dev.type == "cuda":
+                torch.cuda.synchronize(dev)
+            now = time.perf_counter()
+            t[name] = now - clock[0]
+            clock[0] = now
+
+    X = torch.empty((naux, naux), dtype=torch.float32, device=dev)
+    if r == 0:
+        Jd = J_metric.to(dev, torch.float32)
+        X.copy_(_local_metric(Jd) if _local_metric is not None else _metric_inv_half(Jd))
+    Cp = torch.zeros((nbasis, nocc_pad), dtype=torch.float32)
+    Cp[:, :nocc] = C_occ.detach().to("cpu", torch.float32)
+    rows = _eri_rows(nbasis, w, eri_symmetric)[r]
+    part = _half_transform_part(Cp, eri_3c, rows, dev, eri_symmetric, nbasis)
+    mark("chol_upload_2a")
+    if w > 1:
+        iv_r = torch.empty((occ_r, nbasis * naux), dtype=torch.float32, device=dev)
+        _reduce_scatter(iv_r, part, group)
+        del part
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast(X, src, group=group)
+    else:
+        iv_r = part
+    mark("rs_iv_bcast_X")
+
+    CvT = C_vir.detach().T.to(dev, torch.float32).contiguous()  # (nvir, nbasis)
+    ia_r = _bmm(CvT.unsqueeze(0).expand(occ_r, nvir, nbasis), iv_r.reshape(occ_r, nbasis, naux))
+    del iv_r
+    B_r = _mm(ia_r.reshape(occ_r * nvir, naux), X).reshape(occ_r, nvir, naux)
+    del ia_r
+    mark("local_2b_3")
+
+    B_full = (all_gather_rows(B_r, group) if w > 1 else B_r)[:nocc].contiguous()
+    del B_r
+    mark("ag_B")
+    eo = eps_occ.detach().to(dev, torch.float32)
+    ev = eps_vir.detach().to(dev, torch.float32)
+    e = pair_energy(B_full, eo, ev, group)
+    mark("energy")
+    if timings is not None:
+        timings.update(t)
+    return e
 
 
 __all__ = [
     "Grid2D",
     "all_gather_rows",
     "device",
+    "df_mp2_energy",
     "gemm_2d",
     "gemm_col_parallel",
     "gemm_k_parallel",
     "gemm_row_parallel",
     "grid_shape",
+    "pack_tril",
     "pair_energy",
     "shard_2d",
 ]

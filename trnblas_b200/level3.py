@@ -607,10 +607,11 @@ def trsm(
     trans = trans_flag(trans)
     if A.dim() != 2 or A.shape[0] != A.shape[1]:
         raise ValueError(f"trsm: A must be a square matrix, got {tuple(A.shape)}")
-    if A.dtype not in N.KERNEL_DTYPES or B.dtype not in N.KERNEL_DTYPES:
-        return _trsm_torch(alpha, A, B, side, uplo, trans, diag)
     vec = B.dim() == 1
     b = B.unsqueeze(1 if side == "left" else 0) if vec else B
+    if A.dtype not in N.KERNEL_DTYPES or B.dtype not in N.KERNEL_DTYPES:
+        X = _trsm_torch(alpha, A, b, side, uplo, trans, diag)
+        return X.reshape(-1) if vec else X
     if b.dim() != 2:
         raise ValueError(f"trsm: B must be 1-D or 2-D, got {tuple(B.shape)}")
     n = A.shape[0]

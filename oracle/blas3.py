@@ -62,3 +62,24 @@ def relf(x, ref) -> float:
     ref = np.asarray(ref, dtype=np.float64)
     den = np.linalg.norm(ref)
     return float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))
+
+
+def symm(alpha, A, B, beta=0.0, C=None, side="left", uplo="upper", dtype=np.float64):
+    """trnblas/level3.py:196-240: alpha * sym(A) @ B (+ beta C), or B @ sym(A);
+    sym(A) built from A's `uplo` triangle."""
+    A = np.asarray(A, dtype=dtype)
+    S = np.triu(A) + np.triu(A, 1).T if uplo == "upper" else np.tril(A) + np.tril(A, -1).T
+    B = np.asarray(B, dtype=dtype)
+    R = alpha * (S @ B if side == "left" else B @ S)
+    return R + beta * np.asarray(C, dtype=dtype) if (C is not None and beta != 0.0) else R
+
+
+def trmm(alpha, A, B, side="left", uplo="upper", trans=False, diag="nonunit", dtype=np.float64):
+    """trnblas/level3.py:383-417: alpha * op(tri(A)) @ B or alpha * B @ op(tri(A))."""
+    A = np.asarray(A, dtype=dtype)
+    T = np.triu(A) if uplo == "upper" else np.tril(A)
+    if diag == "unit":
+        T = T - np.diag(np.diag(T)) + np.eye(A.shape[0], dtype=dtype)
+    M = T.T if trans else T
+    B = np.asarray(B, dtype=dtype)
+    return alpha * (M @ B if side == "left" else B @ M)

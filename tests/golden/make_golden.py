@@ -19,7 +19,9 @@ outputs of the hot-path functions:
   fp64 on the example's own synthetic inputs, trnblas.parallel.df_mp2_energy
   on one gloo rank (full and packed-symmetric integrals), trnblas.trsm over
   side / uplo / trans / diag, trnblas.metric_inv_half.
-`--only dfmp2` writes just dfmp2.npz.
+- trnblas.symm (side x uplo, with beta and C) and trnblas.trmm (side x uplo
+  x trans x diag) on seeded fp32 inputs (symm_trmm.npz).
+`--only dfmp2` / `--only symm_trmm` writes just that file.
 Inputs that tests can regenerate from a seed are not stored when large.
 The torch / numpy versions used are written into meta.json.
 """
@@ -231,11 +233,39 @@ def dfmp2_cases(trnblas):
     return out
 
 
+def symm_trmm_cases(trnblas):
+    """symm and trmm of the reference on seeded fp32 inputs (CPU torch route)."""
+    out = {}
+    g = torch.Generator().manual_seed(31)
+    n, m = 96, 80
+    A = torch.randn(n, n, generator=g)
+    B = torch.randn(n, m, generator=g)
+    Br = torch.randn(m, n, generator=g)
+    C = torch.randn(n, m, generator=g)
+    Cr = torch.randn(m, n, generator=g)
+    out.update(A=A.numpy(), B=B.numpy(), Br=Br.numpy(), C=C.numpy(), Cr=Cr.numpy())
+    for uplo in ("upper", "lower"):
+        out[f"symm_left_{uplo}"] = trnblas.symm(1.5, A, B, 0.5, C, side="left", uplo=uplo).numpy()
+        out[f"symm_right_{uplo}"] = trnblas.symm(-0.75, A, Br, 2.0, Cr, side="right", uplo=uplo).numpy()
+        for side in ("left", "right"):
+            X = B if side == "left" else Br
+            for trans in (False, True):
+                for diag in ("nonunit", "unit"):
+                    out[f"trmm_{side}_{uplo}_{int(trans)}_{diag}"] = trnblas.trmm(
+                        0.5, A, X, side=side, uplo=uplo, trans=trans, diag=diag).numpy()
+    return out
+
+
 def main():
     trnblas, ozaki, dispatch, multicore = _ref()
-    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "dfmp2":
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only == "dfmp2":
         np.savez_compressed(HERE / "dfmp2.npz", **dfmp2_cases(trnblas))
         print("dfmp2.npz written")
+        return
+    if only == "symm_trmm":
+        np.savez_compressed(HERE / "symm_trmm.npz", **symm_trmm_cases(trnblas))
+        print("symm_trmm.npz written")
         return
     full = "--quick" not in sys.argv
     meta = {

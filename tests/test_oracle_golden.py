@@ -294,3 +294,20 @@ def test_trsm_oracle_matches_reference(side, uplo, trans, diag):
     X = dfmp2.trsm(0.5, A, Bm, side, uplo, trans, diag)
     ref = d[f"trsm_{side}_{uplo}_{int(trans)}_{diag}"]
     assert blas3.relf(ref, X) <= 1e-5
+
+
+# ── symm / trmm ──────────────────────────────────────────────────────────────
+
+
+def test_symm_trmm_oracle_matches_reference():
+    d = load("symm_trmm.npz")
+    A, B, Br, C, Cr = d["A"], d["B"], d["Br"], d["C"], d["Cr"]
+    for uplo in ("upper", "lower"):
+        assert blas3.relf(d[f"symm_left_{uplo}"], blas3.symm(1.5, A, B, 0.5, C, "left", uplo)) <= 1e-6
+        assert blas3.relf(d[f"symm_right_{uplo}"], blas3.symm(-0.75, A, Br, 2.0, Cr, "right", uplo)) <= 1e-6
+        for side in ("left", "right"):
+            X = B if side == "left" else Br
+            for trans in (False, True):
+                for diag in ("nonunit", "unit"):
+                    ref = d[f"trmm_{side}_{uplo}_{int(trans)}_{diag}"]
+                    assert blas3.relf(ref, blas3.trmm(0.5, A, X, side, uplo, trans, diag)) <= 1e-6

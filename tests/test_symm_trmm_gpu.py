@@ -1,0 +1,65 @@
+"""symm and trmm on the GEMM kernel against the reference's outputs
+(tests/golden/symm_trmm.npz) and the fp64 oracle: relF <= 1e-5 (fp32 as
+3xTF32), bf16 <= 1e-2."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import trnblas_b200 as tb
+from oracle import blas3
+
+pytestmark = pytest.mark.gpu
+D = np.load(Path(__file__).resolve().parent / "golden" / "symm_trmm.npz")
+
+
+def _t(name, dev="cuda"):
+    return torch.from_numpy(D[name]).to(dev)
+
+
+@pytest.mark.parametrize("uplo", ["upper", "lower"])
+def test_symm_matches_reference(uplo):
+    L = tb.symm(1.5, _t("A"), _t("B"), 0.5, _t("C"), side="left", uplo=uplo)
+    R = tb.symm(-0.75, _t("A"), _t("Br"), 2.0, _t("Cr"), side="right", uplo=uplo)
+    assert L.dtype == torch.float32 and L.is_cuda
+    assert blas3.relf(L.cpu().numpy(), D[f"symm_left_{uplo}"]) <= 1e-5
+    assert blas3.relf(R.cpu().numpy(), D[f"symm_right_{uplo}"]) <= 1e-5
+    # only the uplo triangle is read: garbage in the other one changes nothing
+    A = _t("A").clone()
+    junk = torch.full_like(A, float("nan"))
+    A = torch.where(torch.ones_like(A, dtype=torch.bool).triu() if uplo == "upper" else torch.ones_like(A, dtype=torch.bool).tril(), A, junk)
+    L2 = tb.symm(1.5, A, _t("B"), 0.5, _t("C"), side="left", uplo=uplo)
+    assert torch.equal(L2, L)
+    # host operands: result on the host
+    Lh = tb.symm(1.5, _t("A", "cpu"), _t("B", "cpu"), 0.5, _t("C", "cpu"), side="left", uplo=uplo)
+    assert Lh.device.type == "cpu" and torch.equal(Lh, L.cpu())
+
+
+@pytest.mark.parametrize("side", ["left", "right"])
+@pytest.mark.parametrize("uplo", ["upper", "lower"])
+@pytest.mark.parametrize("trans", [False, True])
+@pytest.mark.parametrize("diag", ["nonunit", "unit"])
+def test_trmm_matches_reference(side, uplo, trans, diag):
+    X = _t("B") if side == "left" else _t("Br")
+    R = tb.trmm(0.5, _t("A"), X, side=side, uplo=uplo, trans=trans, diag=diag)
+    ref = D[f"trmm_{side}_{uplo}_{int(trans)}_{diag}"]
+    assert blas3.relf(R.cpu().numpy(), ref) <= 1e-5
+    exact = blas3.trmm(0.5, D["A"], X.cpu().numpy(), side, uplo, trans, diag)
+    assert blas3.relf(R.cpu().numpy(), exact) <= 1e-5
+
+
+def test_symm_trmm_bf16_and_large():
+    g = torch.Generator(device="cuda").manual_seed(2)
+    A = torch.randn(1000, 1000, device="cuda", generator=g)
+    B = torch.randn(1000, 777, device="cuda", generator=g)
+    for dt, tol in ((torch.float32, 1e-5), (torch.bfloat16, 1e-2)):
+        S = tb.symm(1.0, A.to(dt), B.to(dt), uplo="lower")
+        ref = blas3.symm(1.0, A.to(dt).float().cpu().numpy(), B.to(dt).float().cpu().numpy(), uplo="lower")
+        assert S.dtype == dt and blas3.relf(S.float().cpu().numpy(), ref) <= tol
+        T = tb.trmm(2.0, A.to(dt), B.to(dt), uplo="upper", trans=True)
+        ref = blas3.trmm(2.0, A.to(dt).float().cpu().numpy(), B.to(dt).float().cpu().numpy(), "left", "upper", True)
+        assert T.dtype == dt and blas3.relf(T.float().cpu().numpy(), ref) <= tol

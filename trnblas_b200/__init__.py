@@ -12,7 +12,7 @@ from . import _native
 from ._flags import diag_flag, side_flag, trans_flag, uplo_flag
 from . import energy, parallel
 from .energy import batched_pair_energy, nki_batched_pair_energy, pair_range_energy
-from .level3 import batched_gemm, gemm, gemm_fp64, metric_inv_half, syrk, trsm
+from .level3 import batched_gemm, gemm, gemm_fp64, metric_inv_half, symm, syrk, trmm, trsm
 
 __version__ = "0.1.0"
 

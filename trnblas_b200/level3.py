@@ -1,5 +1,5 @@
 """BLAS level 3 on B200: gemm, batched_gemm, syrk, gemm_fp64, trsm,
-metric_inv_half.
+metric_inv_half, symm, trmm.
 
 Same signatures, argument meanings, return dtypes and exceptions as the
 reference's trnblas/level3.py (gemm :69-109, batched_gemm :112-134, gemm_fp64
@@ -655,3 +655,72 @@ def metric_inv_half(J: torch.Tensor) -> torch.Tensor:
     eye = torch.eye(J.shape[0], dtype=torch.float32, device=dev)
     X = trsm(1.0, L, eye, uplo="lower", trans=True).to(J.dtype)
     return X.to(home) if home != dev else X
+
+
+# ── symmetric and triangular multiplies (on the GEMM kernel) ─────────────────
+
+
+def _sym_full(A: torch.Tensor, uplo: str) -> torch.Tensor:
+    """The symmetric matrix whose `uplo` triangle (with the diagonal) is A's."""
+    if uplo == "upper":
+        return torch.triu(A) + torch.triu(A, diagonal=1).mT
+    return torch.tril(A) + torch.tril(A, diagonal=-1).mT
+
+
+def symm(
+    alpha: float,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    beta: float = 0.0,
+    C: torch.Tensor | None = None,
+    side: str = "left",
+    uplo: str = "upper",
+) -> torch.Tensor:
+    """Symmetric matrix multiply (trnblas/level3.py:196-240):
+    C = alpha * A @ B + beta * C (side 'left') or alpha * B @ A + beta * C
+    ('right'), A symmetric with only its `uplo` triangle read. The full
+    symmetric operand is formed on the operands' device (one elementwise
+    pass over n x n), then one GEMM on the tcgen05 kernel with alpha, beta and
+    C fused in its epilogue (same C rules as `gemm`)."""
+    side, uplo = side_flag(side), uplo_flag(uplo)
+    if A.dim() != 2 or A.shape[0] != A.shape[1]:
+        raise ValueError(f"symm: A must be a square matrix, got {tuple(A.shape)}")
+    if A.dtype in N.KERNEL_DTYPES and B.dtype == A.dtype:
+        dev = _cuda_device(A, B, C)
+        S = _sym_full(_to(A, dev), uplo)
+        if A.device != dev:
+            r = gemm(alpha, S, _to(B, dev), beta, _to(C, dev)) if side == "left" else gemm(alpha, _to(B, dev), S, beta, _to(C, dev))
+            return r.to(A.device)
+    else:
+        S = _sym_full(A, uplo)
+    return gemm(alpha, S, B, beta, C) if side == "left" else gemm(alpha, B, S, beta, C)
+
+
+def trmm(
+    alpha: float,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    side: str = "left",
+    uplo: str = "upper",
+    trans: bool = False,
+    diag: str = "nonunit",
+) -> torch.Tensor:
+    """Triangular matrix multiply (trnblas/level3.py:383-417):
+    alpha * op(tri(A)) @ B (side 'left') or alpha * B @ op(tri(A)) ('right'),
+    tri(A) the `uplo` triangle of A (diagonal ones for diag 'unit'). The
+    triangle is masked on the operands' device and multiplied on the GEMM
+    kernel; op = transpose is read in place (no transposed copy)."""
+    side, uplo, diag = side_flag(side), uplo_flag(uplo), diag_flag(diag)
+    trans = trans_flag(trans)
+    if A.dim() != 2 or A.shape[0] != A.shape[1]:
+        raise ValueError(f"trmm: A must be a square matrix, got {tuple(A.shape)}")
+    home = A.device
+    dev = _cuda_device(A, B) if A.dtype in N.KERNEL_DTYPES and B.dtype == A.dtype else A.device
+    a = _to(A, dev)
+    tri = torch.triu(a) if uplo == "upper" else torch.tril(a)
+    if diag == "unit":
+        tri.diagonal().fill_(1)
+    mat = tri.mT if trans else tri
+    b = _to(B, dev)
+    r = gemm(alpha, mat, b) if side == "left" else gemm(alpha, b, mat)
+    return r.to(home) if home != dev else r

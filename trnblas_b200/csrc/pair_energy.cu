@@ -28,9 +28,9 @@
 //   X = B_i[R] . B_j[C]^T  ->  X[a, b] = T_ab
 //   Y = B_j[R] . B_i[C]^T  ->  Y[a, b] = T_ba
 // so T_ab and T_ba land in the same TMEM lane and column: no transpose. The
-// epilogue folds X into 64 registers per thread and releases TMEM before the
-// Y pass, then Y, then computes the terms from registers while the next
-// unit's X pass runs. Per (a, b): if the 64-blocks of a and b differ, the
+// epilogue (8 warps, 32 columns each) folds X into registers and releases
+// TMEM before the Y pass, then Y, then computes the terms from registers
+// while the next unit's X pass runs. Per (a, b): if the 64-blocks of a and b differ, the
 // unit accounts for both ordered pairs, [X(2X-Y) + Y(2Y-X)] / D; if they are
 // the same block, X(2X-Y) / D once; a in block 2R+1 with b in block 2R is
 // skipped (unit (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
@@ -198,8 +198,16 @@ __device__ __forceinline__ void pair_mma_role(uint8_t* smem, uint64_t* full_bar,
   }
 }
 
+// Block: warp 0 producer, warp 1 MMA issuer and TMEM owner, warps 2..9
+// epilogue. Two epilogue warps share each TMEM lane quarter (warp w reads
+// lanes 32 (w % 4) .. +31), one taking columns 0..31 of the 64-column block,
+// the other 32..63, so each warp's energy loop (fp64 quotients and sums,
+// latency bound with one warp per scheduler) is half as long.
+constexpr int kPairEpiWarps = 8;
+constexpr int kPairThreads = 32 * (2 + kPairEpiWarps);
+
 template <int KS, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     pair_energy_kernel(const PairParams p) {
   using Cfg = PairCfg<KS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -212,7 +220,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain_bar = acce_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  double* red = reinterpret_cast<double*>(smem + STAGES * Cfg::STAGE_BYTES + 128);  // [4]
+  double* red = reinterpret_cast<double*>(smem + STAGES * Cfg::STAGE_BYTES + 128);  // [kPairEpiWarps]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Abort ab{abort_flag, p.status, p.timeout_ns};
@@ -223,10 +231,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(accf_bar, 1);
-    mbar_init(acce_bar, 4);
+    mbar_init(acce_bar, kPairEpiWarps);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
-    for (int w = 0; w < 4; ++w) red[w] = 0.0;
+    for (int w = 0; w < kPairEpiWarps; ++w) red[w] = 0.0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -300,15 +308,17 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
+    constexpr int NCOL = 64 / (kPairEpiWarps / 4);  // columns per epilogue warp
     const int q = warp & 3;
+    const int col0 = NCOL * ((warp - 2) / 4);
     const int aloc = 32 * q + lane;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + col0;
     double acc = 0.0;  // this thread's fp64 partial sum
     int it = 0;
     bool aborted = false;
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
-      // fold the KS diagonals of one pass into 64 fp32 values (unscaled T)
-      float xt[64], yt[64];
+      // fold the KS diagonals of one pass into NCOL fp32 values (unscaled T)
+      float xt[NCOL], yt[NCOL];
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass, ++it) {
         if (!mbar_wait_warp(accf_bar, it & 1, ab, kTimeoutAccFull)) {
@@ -317,7 +327,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NCOL / 16; ++c) {
           uint32_t v[KS][16];
 #pragma unroll
           for (int d = 0; d < KS; ++d) tmem_ld16(lane_base + d * Cfg::BN + 16 * c, v[d]);
@@ -355,9 +365,9 @@ __global__ void __launch_bounds__(192, 1)
         // shared by every term of the pair, which does not average out.
         const double da = (static_cast<double>(p.eps_occ[i]) + static_cast<double>(p.eps_occ[j])) -
                           static_cast<double>(p.eps_vir[a]);
-        const int b0 = 64 * C;
+        const int b0 = 64 * C + col0;
 #pragma unroll
-        for (int jj = 0; jj < 64; ++jj) {
+        for (int jj = 0; jj < NCOL; ++jj) {
           const int b = b0 + jj;
           if (b < p.nvir) {
             const float X = xt[jj] * pow2f(eia + p.exps[j * p.nvir + b] - 12);
@@ -379,7 +389,11 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) p.partials[blockIdx.x] = ((red[0] + red[1]) + red[2]) + red[3];
+  if (threadIdx.x == 0) {
+    double part = 0.0;
+    for (int w = 0; w < kPairEpiWarps; ++w) part += red[w];  // fixed order
+    p.partials[blockIdx.x] = part;
+  }
   if (warp == 1) {
     __syncwarp();  // lane 0 arrives from the MMA role, 1..31 straight here
     tc_fence_after();
@@ -558,7 +572,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<grid, 192, smem, stream>>>(p);
+  kern<<<grid, kPairThreads, smem, stream>>>(p);
   pair_energy_finish<<<1, 32, 0, stream>>>(partials, grid, energy);
   e = cudaGetLastError();
   return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "pair energy launch");

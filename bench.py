@@ -267,7 +267,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
     g = torch.Generator(device="cuda").manual_seed(5 + 1000 * rank)
     A_sh = (2 * torch.rand(mw, n, device="cuda", generator=g) - 1).to(dtype)
     B_sh = (2 * torch.rand(n, nw, device="cuda", generator=g) - 1).to(dtype)
-    k_chunks = 1 if world == 1 else 4
+    k_chunks = 1  # gather, then one GEMM: NCCL kernels running beside the persistent GEMM slow both
     events = []
 
     def step():

@@ -73,7 +73,7 @@ def _primitives(rank, world, tp):
 
 def _gemm2d(rank, world, tp):
     g = torch.Generator().manual_seed(6)
-    M, K, N = 16 * world, 12, 24 * world
+    M, K, N = 16 * world, 48, 24 * world
     A = torch.randn(M, K, generator=g)
     B = torch.randn(K, N, generator=g)
     grid = tp.Grid2D()

@@ -183,11 +183,61 @@ def shard_2d(A: torch.Tensor, B: torch.Tensor, grid: Grid2D):
     return A[grid.rank * mw : (grid.rank + 1) * mw], B[:, s * nw : (s + 1) * nw]
 
 
+def _panel_gemm(a: torch.Tensor, b_stack: torch.Tensor, pieces: int, C: torch.Tensor, beta: float) -> None:
+    """C[:, r*nw:(r+1)*nw] = a @ b_stack[r] + beta * (same), r < pieces, in
+    place: one batched launch of the GEMM kernel with A broadcast (batch
+    stride 0), B pieces kc x nw stacked along dim 0 and D / C the column slices
+    of C (batch stride nw, leading dimension pieces * nw). Each output element
+    is read (beta = 1) and written by the same epilogue thread, so C may be
+    its own accumulator."""
+    from . import _native as N
+
+    M, kc = a.shape
+    nw = b_stack.shape[1]
+    if _local_mm is not None:
+        for r in range(pieces):
+            blk = C[:, r * nw : (r + 1) * nw]
+            part = _local_mm(a, b_stack[r * kc : (r + 1) * kc])
+            blk.copy_(part if beta == 0.0 else blk + part)
+        return
+    code = N.dtype_code(a.dtype)
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    b_stack = b_stack.contiguous()
+    lda, ldc = a.stride(0), C.stride(0)
+    es = a.element_size()
+    tma_ok = all(v % 16 == 0 for v in (lda * es, nw * es, kc * nw * es, a.data_ptr(), b_stack.data_ptr()))
+    if code != N.F32 and not tma_ok:
+        # ragged 16-bit shapes (strides off the 16-byte TMA grid): per slab
+        # through the public GEMM, which pads such operands
+        for r in range(pieces):
+            blk = C[:, r * nw : (r + 1) * nw]
+            part = _gemm(1.0, a, b_stack[r * kc : (r + 1) * kc])
+            if beta == 0.0:
+                blk.copy_(part)
+            else:
+                blk.add_(part)
+        return
+    dev = a.device
+    ws_bytes = N.lib().trnblas_gemm_workspace_size(code, pieces, M, nw, kc, 0, kc * nw)
+    ws = N.workspace(ws_bytes, dev)
+    rc = N.lib().trnblas_gemm(
+        code, pieces, M, nw, kc, 1.0,
+        N.ptr(a), lda, 0, 0,
+        N.ptr(b_stack), nw, kc * nw, 0,
+        float(beta), N.ptr(C) if beta != 0.0 else None, ldc, nw,
+        N.ptr(C), ldc, nw,
+        N.ptr(ws), ws_bytes, N.stream_ptr(dev),
+    )
+    N.check(rc, "trnblas_gemm")
+    N.count_launches(3 if code == N.F32 else 1)
+
+
 def gemm_2d(
     A_shard: torch.Tensor,
     B_shard: torch.Tensor,
     grid: Grid2D,
-    k_chunks: int = 4,
+    k_chunks: int = 1,
     kernel_events: list | None = None,
 ) -> torch.Tensor:
     """This rank's (M/pr) x (N/pc) block of C = A @ B on a pr x pc grid.
@@ -195,42 +245,51 @@ def gemm_2d(
     A_shard (M/w, K): rows [rank * M/w, (rank+1) * M/w) of A.
     B_shard (K, N/w): columns of B shard index c * pr + r.
     Grid row r gathers the A shards of its pc ranks (rows of block r) and grid
-    column c the B shards of its pr ranks (columns of block c), both over NCCL
-    in `k_chunks` K-chunks on a side stream while the local GEMM of the
-    previous chunk runs; chunk products accumulate through the fused beta = 1
-    epilogue. Returns the C block (rows `grid.block_rows(M)`, columns
-    `grid.block_cols(N)`). A grid row / column of one rank needs no gather.
-    `kernel_events`, when given, receives a (start, end) CUDA event pair
-    around each local GEMM launch on the launching stream.
+    column c the B shards of its pr ranks (columns of block c) over NCCL, in
+    `k_chunks` K-chunks on a side stream, each chunk's gather issued before the
+    previous chunk's GEMM. B shards are gathered as they lie (kc x N/w row
+    slabs, stacked along dim 0: no transposed copies) and multiplied by one
+    batched launch that writes each slab's columns of the C block in place;
+    later chunks accumulate through the fused beta = 1 epilogue. Returns the C
+    block (rows `grid.block_rows(M)`, columns `grid.block_cols(N)`). A grid
+    row / column of one rank needs no gather. `kernel_events`, when given,
+    receives a (start, end) CUDA event pair around each local GEMM launch on
+    the launching stream.
     """
     pr, pc = grid.pr, grid.pc
     mw, K = A_shard.shape
     K2, nw = B_shard.shape
     if K != K2:
         raise ValueError(f"gemm_2d: A shard has K={K}, B shard K={K2}")
-    k_chunks = max(1, min(int(k_chunks), max(K, 1)))
-    bounds = [K * i // k_chunks for i in range(k_chunks + 1)]
+    k_chunks = max(1, min(int(k_chunks), max(K // 16, 1)))
+    # chunk bounds on multiples of 16 elements, so gathered chunks keep
+    # 16-byte aligned rows for the TMA loads
+    bounds = [min(K, (K * i // k_chunks) // 16 * 16) for i in range(k_chunks)] + [K]
     dev = A_shard.device
     cuda = dev.type == "cuda"
     comm = torch.cuda.Stream(dev) if cuda else None
     main = torch.cuda.current_stream(dev) if cuda else None
+    A_shard = A_shard if A_shard.stride(1) == 1 else A_shard.contiguous()
+    B_shard = B_shard.contiguous()
 
     def gather_chunk(k0, k1):
+        whole = k0 == 0 and k1 == K
         if pc == 1:
             a_full = A_shard[:, k0:k1]
         else:
-            a_part = A_shard[:, k0:k1].contiguous()
+            a_part = A_shard if whole else A_shard[:, k0:k1].contiguous()
             a_full = torch.empty((pc * mw, k1 - k0), dtype=A_shard.dtype, device=dev)
             dist.all_gather_into_tensor(a_full, a_part, group=grid.row_group)
         if pr == 1:
-            b_full = B_shard[k0:k1].T  # a transposed view: the kernel reads it as is
+            b_full = B_shard[k0:k1]
         else:
-            b_part = B_shard[k0:k1].T.contiguous()  # (nw, kc)
-            b_full = torch.empty((pr * nw, k1 - k0), dtype=B_shard.dtype, device=dev)
-            dist.all_gather_into_tensor(b_full, b_part, group=grid.col_group)
-        return a_full, b_full  # b_full holds the B block transposed (N_blk, kc)
+            b_full = torch.empty((pr * (k1 - k0), nw), dtype=B_shard.dtype, device=dev)
+            dist.all_gather_into_tensor(b_full, B_shard[k0:k1], group=grid.col_group)
+        return a_full, b_full  # b_full: pr slabs (kc x nw) of the column block
 
-    C = None
+    C = torch.empty((pc * mw, pr * nw), dtype=A_shard.dtype, device=dev)
+    if K == 0:
+        return C.zero_()
     pending, events = [], []
     if cuda:
         comm.wait_stream(main)
@@ -248,24 +307,18 @@ def gemm_2d(
                 pending.append(gather_chunk(bounds[j], bounds[j + 1]))
         if cuda:
             main.wait_event(events[i])
-        a_full, b_full_t = pending[i]
+        a_full, b_full = pending[i]
         if cuda:
             a_full.record_stream(main)
-            b_full_t.record_stream(main)
-        if _local_mm is not None:
-            part = _local_mm(a_full, b_full_t.T)
-            C = part if C is None else C + part
-        else:
-            if kernel_events is not None:
-                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                ev0.record(main)
-            C = _gemm(1.0, a_full, b_full_t, 1.0 if C is not None else 0.0, C, transB=True)
-            if kernel_events is not None:
-                ev1.record(main)
-                kernel_events.append((ev0, ev1))
+            b_full.record_stream(main)
+        if kernel_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(main)
+        _panel_gemm(a_full, b_full, pr, C, 0.0 if i == 0 else 1.0)
+        if kernel_events is not None:
+            ev1.record(main)
+            kernel_events.append((ev0, ev1))
         pending[i] = None
-    if C is None:
-        C = torch.zeros((pc * mw, pr * nw), dtype=A_shard.dtype, device=dev)
     return C
 
 

@@ -180,6 +180,10 @@ def _gemm_public(alpha, a, b, beta, C):
         return r + beta * C if (C is not None and beta != 0.0) else r
     home = a.device
     dev = _cuda_device(a, b, C)
+    if home.type == "cpu" and b.device.type == "cpu":
+        r = _gemm_host_streamed(alpha, a, b, beta, C, dev)
+        if r is not None:
+            return r
     a2, b2 = _to(a, dev), _to(b, dev)
     squeeze = []
     if a2.dim() == 1:
@@ -199,6 +203,63 @@ def _gemm_public(alpha, a, b, beta, C):
     if not fuse:
         r = _add_c(r, beta, Cd)
     return r.to(home) if home != dev else r
+
+
+# Host operands of at least this many flops stream through the GPU in row
+# blocks of about STREAM_BLOCK_BYTES of A.
+STREAM_MIN_FLOPS = 2.0 ** 34
+STREAM_BLOCK_BYTES = 128 << 20
+
+
+def _gemm_host_streamed(alpha, a, b, beta, C, dev):
+    """alpha a @ b (+ beta C) for host operands, streamed: B is uploaded once,
+    then row blocks of A (and of a fused C) go up on one stream, their GEMMs
+    run on the current stream and the finished rows of the result come down
+    on a third, so PCIe uploads, downloads (full duplex) and the tensor cores
+    overlap instead of running one after another. Returns a host tensor
+    (pinned, from torch's caching host allocator) once its data has arrived,
+    or None when the problem is small or not a plain 2-D row-major product
+    (the caller then takes the one-shot path). Pageable inputs work but their
+    copies cannot overlap."""
+    if a.dim() != 2 or b.dim() != 2 or a.stride(1) != 1 or a.shape[1] != b.shape[0]:
+        return None
+    M, K = a.shape
+    Nn = b.shape[1]
+    if 2.0 * M * Nn * K < STREAM_MIN_FLOPS or M < 512:
+        return None
+    fuse = C is not None and beta != 0.0
+    if fuse and not (isinstance(C, torch.Tensor) and C.device.type == "cpu" and tuple(C.shape) == (M, Nn)
+                     and C.dtype == a.dtype and C.stride(1) == 1):
+        return None
+    es = a.element_size()
+    mb = max(128, min(M, STREAM_BLOCK_BYTES // max(K * es, 1)) // 128 * 128)
+    main = torch.cuda.current_stream(dev)
+    up = torch.cuda.Stream(dev)
+    down = torch.cuda.Stream(dev)
+    out = torch.empty((M, Nn), dtype=a.dtype, pin_memory=True)
+    up.wait_stream(main)
+    with torch.cuda.stream(up):
+        b_d = b.to(dev, non_blocking=True)
+    for r0 in range(0, M, mb):
+        r1 = min(r0 + mb, M)
+        with torch.cuda.stream(up):
+            a_i = a[r0:r1].to(dev, non_blocking=True)
+            c_i = C[r0:r1].to(dev, non_blocking=True) if fuse else None
+        ready = torch.cuda.Event()
+        ready.record(up)
+        main.wait_event(ready)
+        for t in (a_i, b_d, c_i):
+            if t is not None:
+                t.record_stream(main)
+        r = _gemm2d(a_i, b_d, alpha, beta if fuse else 0.0, c_i)
+        done = torch.cuda.Event()
+        done.record(main)
+        down.wait_event(done)
+        with torch.cuda.stream(down):
+            out[r0:r1].copy_(r, non_blocking=True)
+        r.record_stream(down)
+    down.synchronize()
+    return out
 
 
 def _flat_batch(x: torch.Tensor, batch: tuple, esize: int, f32: bool):

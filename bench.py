@@ -416,9 +416,25 @@ def run_pair(args, rank, world, gpu, nocc, nvir, naux, steps=None, warmup=None):
     pk, src = peaks()
     which = "bf16_tflops_sustained" if kern_ms >= 1000.0 else "bf16_tflops"
     int8_peak = 2.0 * pk[which]
+    # e2e: the public call on pinned host inputs (each rank uploads B)
+    Bh = B.cpu().pin_memory()
+    eoh, evh = eo.cpu(), ev.cpu()
     del B
     torch.cuda.empty_cache()
+
+    def e2e_step():
+        if world == 1:
+            out["e2e"] = float(energy.batched_pair_energy(Bh, eoh, evh))
+        else:
+            out["e2e"] = tp.pair_energy(Bh, eoh, evh)
+
+    e2e_ms, _ = timed_steps(e2e_step, max(1, min(steps, 2)), 1, world, gpu)
+    e2e_info = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(Bh.numel() * 4 * world),
+                "d2h_bytes_per_step": 8 * world,
+                "path": "trnblas_b200.batched_pair_energy / parallel.pair_energy on pinned host B"}
+    del Bh
     return {
+        "e2e": e2e_info,
         "ms_per_step": round(ms, 3),
         "energy": E,
         "tflops_sym_count": round(sym_flops / (ms / 1e3) / 1e12, 2),
@@ -494,7 +510,7 @@ def run_ours(args, rank, world, gpu):
             "config": {"workload": args.workload, **r["config"]},
             "roofline": {"bound": "tensor", "achieved": r["int8_tops_achieved"], "peak": r["int8_peak_tops"],
                          "unit": "TOP/s (int8)", "frac": r["int8_frac"], "traffic": read_traffic(f"pair_energy_{args.workload}")},
-            "clocks": r["clocks"], "gpu_launches": r["gpu_launches"], "detail": r,
+            "clocks": r["clocks"], "gpu_launches": r["gpu_launches"], "e2e": r["e2e"], "detail": r,
         }
         if rank == 0 and world == 1:
             ms, th, sample = cpu_pair_sample(*dims)
@@ -633,6 +649,7 @@ def run_single(args, rank, world, gpu):
         flops = 64 * 2.0 * 512 ** 3
     elif wl == "syrk":
         A = torch.randn(4096, 4096, device="cuda", generator=g) / 64
+        B = None
         fn = lambda: tb.syrk(1.0, A, uplo="lower")  # noqa: E731
         flops = 4096 * 4097 * 4096.0
     else:  # gemm_fp64, config 4
@@ -653,6 +670,27 @@ def run_single(args, rank, world, gpu):
             "data": "synthetic (seeded, device generator)", "config": {"workload": wl, "replicas": world},
             "clocks": clocks, "gpu_launches": launches}
     line["roofline"] = single_roofline(wl, A, B, flops)
+    # e2e: the same public call on pinned host operands, result back on the host
+    Ah = A.cpu().pin_memory()
+    Bh = B.cpu().pin_memory() if B is not None else None
+    host_fn = {
+        "gemm_fp64": lambda: tb.gemm_fp64(Ah, Bh),
+        "batched": lambda: tb.batched_gemm(1.0, Ah, Bh),
+        "syrk": lambda: tb.syrk(1.0, Ah, uplo="lower"),
+    }.get(wl, lambda: tb.gemm(1.0, Ah, Bh))
+    res = {}
+
+    def e2e_step():
+        res.pop("r", None)
+        res["r"] = host_fn()
+
+    e2e_ms, _ = timed_steps(e2e_step, max(2, min(args.steps, 5)), 3, world, gpu)
+    out_bytes = res["r"].numel() * res["r"].element_size()
+    line["e2e"] = {"value": round(flops / (e2e_ms / 1e3) / 1e12 * world, 2), "unit": "TFLOP/s",
+                   "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": int((Ah.numel() + (Bh.numel() if Bh is not None else 0)) * Ah.element_size() * world),
+                   "d2h_bytes_per_step": int(out_bytes * world),
+                   "path": "the same public call on pinned host operands"}
     return line
 
 

@@ -90,7 +90,7 @@ def batched_pair_energy(B: torch.Tensor, eps_occ: torch.Tensor, eps_vir: torch.T
     """
     home = B.device
     e = pair_range_energy(B, eps_occ, eps_vir)
-    return e.to(home) if home != e.device else e
+    return e.to(home) if home != e.device else e  # a 0-d result: nothing to stream
 
 
 # The reference's name for the same entry point.

@@ -40,6 +40,21 @@ def _cuda_device(*tensors: torch.Tensor) -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def _home(r: torch.Tensor, home: torch.device, dev: torch.device) -> torch.Tensor:
+    """The result on the caller's device. A host result comes down into
+    pinned memory from torch's caching host allocator (a full-speed DMA; a
+    pageable destination is staged and several times slower) and is returned
+    once its data has arrived."""
+    if home == dev:
+        return r
+    if home.type != "cpu" or r.numel() == 0:
+        return r.to(home)
+    out = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
+    out.copy_(r, non_blocking=True)
+    torch.cuda.current_stream(r.device).synchronize()
+    return out
+
+
 def _to(t, dev):
     if t is None or not isinstance(t, torch.Tensor):
         return t
@@ -202,7 +217,7 @@ def _gemm_public(alpha, a, b, beta, C):
         r = r.squeeze(d)
     if not fuse:
         r = _add_c(r, beta, Cd)
-    return r.to(home) if home != dev else r
+    return _home(r, home, dev)
 
 
 # Host operands of at least this many flops stream through the GPU in row
@@ -359,7 +374,7 @@ def _batched(alpha, a, b, beta, C):
         r = out
     if not fuse:
         r = _add_c(r, beta, Cd)
-    return r.to(home) if home != dev else r
+    return _home(r, home, dev)
 
 
 def batched_gemm(
@@ -486,7 +501,7 @@ def syrk(
             R = S + beta * _sym_from_triangle(Cd, _resolve_syrk_uplo(Cd, uplo))
         else:
             R = _symmetrize(S + beta * Cd) if add else S
-        return R.to(home) if home != dev else R
+        return _home(R, home, dev)
     if square_c:
         u = _resolve_syrk_uplo(Cd, uplo)
         if Cd.dtype == a2.dtype:
@@ -497,7 +512,7 @@ def syrk(
         R = _syrk_kernel(a2, alpha, 0.0, None, 0)
         if add:
             R = _symmetrize(R + beta * Cd)
-    return R.to(home) if home != dev else R
+    return _home(R, home, dev)
 
 
 # ── fp64-class GEMM (Ozaki on the int8 tensor cores) ─────────────────────────
@@ -593,7 +608,7 @@ def gemm_fp64(
         r = torch.matmul(a, b)
     else:
         r = _gemm_fp64_device(a, b, k)
-    return r.to(home) if home != dev else r
+    return _home(r, home, dev)
 
 
 # ── triangular solve and the density-fitting metric factor ──────────────────
@@ -689,7 +704,7 @@ def trsm(
     if vec:
         X = X.reshape(-1)
     X = X.to(B.dtype)
-    return X.to(home) if home != dev else X
+    return _home(X, home, dev)
 
 
 def metric_inv_half(J: torch.Tensor) -> torch.Tensor:
@@ -715,7 +730,7 @@ def metric_inv_half(J: torch.Tensor) -> torch.Tensor:
     L = torch.linalg.cholesky(_to(J, dev).to(torch.float32))
     eye = torch.eye(J.shape[0], dtype=torch.float32, device=dev)
     X = trsm(1.0, L, eye, uplo="lower", trans=True).to(J.dtype)
-    return X.to(home) if home != dev else X
+    return _home(X, home, dev)
 
 
 # ── symmetric and triangular multiplies (on the GEMM kernel) ─────────────────
@@ -784,4 +799,4 @@ def trmm(
     mat = tri.mT if trans else tri
     b = _to(B, dev)
     r = gemm(alpha, mat, b) if side == "left" else gemm(alpha, b, mat)
-    return r.to(home) if home != dev else r
+    return _home(r, home, dev)

@@ -227,6 +227,43 @@ def cpu_gemm_sample(n: int, dtype: torch.dtype, budget_s: float = 12.0):
     return 2.0 * rows * n * n / dt / 1e12, threads, f"{rows} x {n} rows of the {n}^3 product, {dtype}"
 
 
+def cpu_single_sample(wl: str, budget_s: float = 10.0):
+    """TFLOP/s of the reference's host route (torch on the CPU, all threads)
+    for a single-GPU workload, on a bounded sample: config 2a batched fp32
+    (a subset of the 64 batch entries), config 2b syrk (A @ A^T on a row
+    sample, lower-triangle flops), config 4 gemm_fp64 (fp64 matmul on a row
+    sample: the reference's CPU gemm_fp64 is host BLAS), 8192^3 bf16/fp32."""
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(7)
+    if wl == "batched":
+        A = torch.randn(64, 512, 512, generator=g)
+        B = torch.randn(64, 512, 512, generator=g)
+        torch.matmul(A[:2], B[:2])
+        t0, nb = time.perf_counter(), 0
+        while time.perf_counter() - t0 < budget_s / 2 and nb < 64:
+            torch.matmul(A[nb:nb + 8], B[nb:nb + 8])
+            nb += 8
+        dt = time.perf_counter() - t0
+        return {"value": round(nb * 2.0 * 512 ** 3 / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+                "kind": "port", "sample": f"{nb} of 64 batch entries, torch CPU bmm fp32 (the reference's host route)"}
+    if wl == "syrk":
+        n = 4096
+        A = torch.randn(n, n, generator=g) / 64
+        rows = 512
+        torch.matmul(A[:64], A.T)
+        t0 = time.perf_counter()
+        torch.matmul(A[:rows], A.T)
+        dt = time.perf_counter() - t0
+        # the reference computes the full square then symmetrises: time per full product
+        full_s = dt * n / rows
+        return {"value": round(n * (n + 1) * n / full_s / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+                "kind": "port", "sample": f"{rows} of {n} rows of A @ A^T (torch CPU fp32, the reference's full-square route), lower-triangle flops"}
+    dt_, n = (torch.float64, 4096) if wl == "gemm_fp64" else ((torch.bfloat16 if wl.endswith("bf16") else torch.float32), 8192)
+    v, th, sample = cpu_gemm_sample(n, dt_, budget_s=budget_s)
+    return {"value": round(v, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
+            "sample": sample + (" (host fp64 BLAS: the reference's CPU gemm_fp64 route)" if wl == "gemm_fp64" else " (torch CPU matmul)")}
+
+
 def cpu_pair_sample(nocc, nvir, naux, budget_s: float = 12.0):
     """Energy-step ms of the reference's chunked CPU energy (oracle restatement,
     fp32 torch on the host), extrapolated from a pair-count sample."""
@@ -691,6 +728,8 @@ def run_single(args, rank, world, gpu):
                    "h2d_bytes_per_step": int((Ah.numel() + (Bh.numel() if Bh is not None else 0)) * Ah.element_size() * world),
                    "d2h_bytes_per_step": int(out_bytes * world),
                    "path": "the same public call on pinned host operands"}
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_single_sample(wl)
     return line
 
 
@@ -771,6 +810,12 @@ def reference_arm(args, world):
                 "steps": 1, "warmup": 1, "config": {"workload": args.workload},
                 "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample},
                 "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload in ("batched", "syrk", "gemm_fp64"):
+        cb = cpu_single_sample(args.workload, budget_s=8.0)
+        return {"impl": "reference", "metric": f"{args.workload} TFLOP/s", "value": cb["value"], "unit": "TFLOP/s",
+                "higher_is_better": True, "n_gpus": world, "steps": 1, "warmup": 1,
+                "config": {"workload": args.workload}, "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     dt = torch.float32 if args.workload in ("gemm_fp32", "gemm8192_fp32") else torch.bfloat16
     n = 32768 if args.workload in ("spmd", "gemm_fp32") else 8192
     vals = []

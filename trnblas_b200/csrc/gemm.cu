@@ -56,6 +56,99 @@ __global__ void split_tf32_kernel(const float* __restrict__ X, long long rs, lon
   }
 }
 
+// The same split for a row-major source (K contiguous, ks == 1), where no
+// transpose is needed: one thread per 4 consecutive k of a row, float4 loads
+// (`vec`: row and batch strides multiples of 4, 16-byte aligned base; else
+// guarded scalar loads) and float4 stores of hi / lo.
+__device__ __forceinline__ void split1(float x, float& h, float& l) {
+  h = tf32_rne(x);
+  l = ((__float_as_uint(x) & 0x7F800000u) == 0x7F800000u) ? 0.0f : x - h;
+}
+
+__global__ void split_tf32_rows_kernel(const float* __restrict__ X, long long rs, long long bs,
+                                       int R, int K, int kp, long long obs, int vec,
+                                       float* __restrict__ hi, float* __restrict__ lo) {
+  const int kq = kp >> 2;
+  const long long b = blockIdx.z;
+  for (int r = blockIdx.y * blockDim.y + threadIdx.y; r < R; r += gridDim.y * blockDim.y) {
+    const float* row = X + b * bs + static_cast<long long>(r) * rs;
+    const long long o0 = b * obs + static_cast<long long>(r) * kp;
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < kq; q += gridDim.x * blockDim.x) {
+      const int k = q << 2;
+      float4 x;
+      if (vec && k + 3 < K) {
+        x = __ldg(reinterpret_cast<const float4*>(row + k));
+      } else {
+        x.x = k < K ? __ldg(row + k) : 0.0f;
+        x.y = k + 1 < K ? __ldg(row + k + 1) : 0.0f;
+        x.z = k + 2 < K ? __ldg(row + k + 2) : 0.0f;
+        x.w = k + 3 < K ? __ldg(row + k + 3) : 0.0f;
+      }
+      float4 h, l;
+      split1(x.x, h.x, l.x);
+      split1(x.y, h.y, l.y);
+      split1(x.z, h.z, l.z);
+      split1(x.w, h.w, l.w);
+      *reinterpret_cast<float4*>(hi + o0 + k) = h;
+      *reinterpret_cast<float4*>(lo + o0 + k) = l;
+    }
+  }
+}
+
+// The transposing split for a source whose rows are contiguous across r
+// (rs == 1, e.g. a row-major K x N B operand read as op(B)^T): 64 (k) x 64 (r)
+// tiles through shared memory, float4 loads along r and float4 stores of
+// hi / lo along k. Needs ks % 4 == 0, bs % 4 == 0 and a 16-byte aligned base;
+// edges are guarded element by element.
+__global__ void split_tf32_t64_kernel(const float* __restrict__ X, long long ks, long long bs,
+                                      int R, int K, int kp, long long obs,
+                                      float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[64][65];  // [k][r]
+  const int k0 = blockIdx.x * 64;
+  const int r0 = blockIdx.y * 64;
+  const long long b = blockIdx.z;
+  const float* Xb = X + b * bs;
+  const int t = threadIdx.x;  // 256
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = t + 256 * i;  // 1024 float4 slots: 64 k rows x 16 r-quads
+    const int kk = idx >> 4, rq = (idx & 15) << 2;
+    const int k = k0 + kk, r = r0 + rq;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < K) {
+      const float* src = Xb + static_cast<long long>(k) * ks + r;
+      if (r + 3 < R) {
+        v = __ldg(reinterpret_cast<const float4*>(src));
+      } else {
+        v.x = r < R ? __ldg(src) : 0.f;
+        v.y = r + 1 < R ? __ldg(src + 1) : 0.f;
+        v.z = r + 2 < R ? __ldg(src + 2) : 0.f;
+      }
+    }
+    tile[kk][rq] = v.x;
+    tile[kk][rq + 1] = v.y;
+    tile[kk][rq + 2] = v.z;
+    tile[kk][rq + 3] = v.w;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = t + 256 * i;  // 64 r rows x 16 k-quads
+    const int rr = idx >> 4, kq = (idx & 15) << 2;
+    const int r = r0 + rr, k = k0 + kq;
+    if (r < R && k < kp) {
+      float4 h, l;
+      split1(tile[kq][rr], h.x, l.x);
+      split1(tile[kq + 1][rr], h.y, l.y);
+      split1(tile[kq + 2][rr], h.z, l.z);
+      split1(tile[kq + 3][rr], h.w, l.w);
+      const long long o = b * obs + static_cast<long long>(r) * kp + k;
+      *reinterpret_cast<float4*>(hi + o) = h;
+      *reinterpret_cast<float4*>(lo + o) = l;
+    }
+  }
+}
+
 // D = beta * C (K == 0): an empty sum times alpha is zero.
 __global__ void scale_c_kernel(int out_kind, long long batch, int M, int N, float beta,
                                const void* C, long long ldc, long long strideC, void* D,
@@ -129,6 +222,28 @@ int check_dims(long long batch, long long M, long long N, long long K) {
 int launch_split(const float* X, long long rs, long long ks, long long bs, long long nb,
                  long long R, long long K, float* hi, float* lo, cudaStream_t stream) {
   const long long kp = round_up(std::max<long long>(K, 1), 4);
+  if (ks == 1 && R <= (1ll << 31) - 1 && nb <= 65535) {
+    const int vec = (rs % 4 == 0) && (bs % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0);
+    const long long kq = kp / 4;
+    dim3 blk(64, 4);
+    dim3 g(static_cast<unsigned>(std::min<long long>(ceil_div(kq, 64), 1024)),
+           static_cast<unsigned>(std::min<long long>(ceil_div(R, 4), 65535)), static_cast<unsigned>(nb));
+    split_tf32_rows_kernel<<<g, blk, 0, stream>>>(X, rs, bs, static_cast<int>(R), static_cast<int>(K),
+                                                  static_cast<int>(kp), R * kp, vec, hi, lo);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "split kernel launch");
+    return TRNBLAS_OK;
+  }
+  if (rs == 1 && ks % 4 == 0 && bs % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
+      ceil_div(R, 64) <= 65535 && nb <= 65535) {
+    dim3 g(static_cast<unsigned>(ceil_div(kp, 64)), static_cast<unsigned>(ceil_div(R, 64)),
+           static_cast<unsigned>(nb));
+    split_tf32_t64_kernel<<<g, 256, 0, stream>>>(X, ks, bs, static_cast<int>(R), static_cast<int>(K),
+                                                 static_cast<int>(kp), R * kp, hi, lo);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "split kernel launch");
+    return TRNBLAS_OK;
+  }
   dim3 grid(static_cast<unsigned>(ceil_div(kp, 32)), static_cast<unsigned>(ceil_div(R, 32)),
             static_cast<unsigned>(nb));
   if (grid.y > 65535 || grid.z > 65535) {

@@ -1,6 +1,6 @@
 """Benchmark of the trnblas_b200 hot path (one JSON line on rank 0).
 
-Default workload (the metric's "1/2/4/8 B200" setting):
+Default workload (benchmark case 5, the headline "1/2/4/8 B200" setting):
 the 2-D output-block sharded GEMM C = A @ B, M = N = K = 32768, bf16
 (`trnblas_b200.parallel.gemm_2d`), one step = the whole GEMM over all ranks;
 value = whole-job TFLOP/s. The same line carries the DF-MP2 pair-energy step
@@ -15,7 +15,7 @@ benchmark shape nbasis/nocc/naux = 768/96/2304).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
 
-Inputs are seeded synthetic tensors with the BASELINE shapes and
+Inputs are seeded synthetic tensors with the benchmark cases' shapes and
 distributions, generated on the device (inputs far larger than L2, so no L2
 flush is needed between steps). Timing: CUDA events on the launching stream,
 barrier + synchronize around the K timed steps, max over ranks.
@@ -358,7 +358,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16" if dtype == torch.bfloat16 else "f32 (3xTF32 on tensor cores)",
-        "data": "synthetic (seeded uniform[-1,1] on device, BASELINE config 5 shapes)",
+        "data": "synthetic (seeded uniform[-1,1] on device, benchmark case 5 shapes)",
         "config": {
             "workload": f"config5a spmd gemm {n}^3",
             "M": n, "N": n, "K": n, "grid": f"{pr}x{pc}", "k_chunks": k_chunks,
@@ -543,7 +543,7 @@ def run_ours(args, rank, world, gpu):
             "value": r["ms_per_step"], "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 (5 Ozaki slices, exact int32) + fp64 reduction",
-            "data": "synthetic (BASELINE recipe, device generator)",
+            "data": "synthetic (benchmark recipe, device generator)",
             "config": {"workload": args.workload, **r["config"]},
             "roofline": {"bound": "tensor", "achieved": r["int8_tops_achieved"], "peak": r["int8_peak_tops"],
                          "unit": "TOP/s (int8)", "frac": r["int8_frac"], "traffic": read_traffic(f"pair_energy_{args.workload}")},

@@ -103,7 +103,7 @@ def pair_ranges(nocc: int, parts: int) -> list[tuple[int, int]]:
 
 
 def make_inputs(nocc: int, nvir: int, naux: int, seed: int, sigma: float = 0.05):
-    """Synthetic DF-MP2 inputs of the BASELINE recipe: B ~ N(0, sigma^2)
+    """Synthetic DF-MP2 inputs of the benchmark recipe: B ~ N(0, sigma^2)
     (nocc, nvir, naux) fp32, eps_occ sorted U[-20, -0.3], eps_vir sorted U[0.1, 5],
     drawn with torch.Generator(seed) in this order."""
     import torch

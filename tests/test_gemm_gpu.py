@@ -1,7 +1,7 @@
 """GEMM, batched GEMM and SYRK on the B200 kernels (through the C ABI via the
 public API) against the oracle / an fp64 product of the same inputs.
 
-Gates: relative Frobenius error <= 1e-5 for fp32
+Gates (the path's accuracy targets): relative Frobenius error <= 1e-5 for fp32
 (3xTF32), <= 1e-2 for bf16; fp16 is held to 2e-3 (its output rounding).
 """
 
@@ -57,7 +57,7 @@ def test_gemm_golden_reference_cases():
 
 
 def test_config1_against_reference_samples():
-    """BASELINE config 1 (fp32 1024^3, transA, beta 0.5, seed 0) vs the reference's output."""
+    """Benchmark case 1 (fp32 1024^3, transA, beta 0.5, seed 0) vs the reference's output."""
     c = np.load("tests/golden/config1.npz")
     gen = torch.Generator().manual_seed(0)
     A, B, C = (2 * torch.rand(1024, 1024, generator=gen) - 1 for _ in range(3))
@@ -114,7 +114,7 @@ def test_mixed_dtypes_raise():
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 def test_batched_config2(dt):
-    """BASELINE config 2a: batch 64 of 512^3 (N(0,1), seed 1), one launch."""
+    """Benchmark case 2a: batch 64 of 512^3 (N(0,1), seed 1), one launch."""
     gen = torch.Generator().manual_seed(1)
     A = torch.randn(64, 512, 512, generator=gen).to(dt)
     B = torch.randn(64, 512, 512, generator=gen).to(dt)
@@ -163,7 +163,7 @@ def test_syrk_golden_reference_cases():
 
 
 def test_syrk_config2_lower():
-    """BASELINE config 2b: n = k = 4096, uplo lower, A ~ N(0, 1/k), seed 2."""
+    """Benchmark case 2b: n = k = 4096, uplo lower, A ~ N(0, 1/k), seed 2."""
     gen = torch.Generator().manual_seed(2)
     A = (torch.randn(4096, 4096, generator=gen) / 64.0).to(DEV)
     out = tb.syrk(1.0, A, uplo="lower")

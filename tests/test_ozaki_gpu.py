@@ -70,7 +70,7 @@ def test_gemm_fp64_slices_and_layouts(k, ta, tbb):
 
 
 def test_gemm_fp64_config4_accuracy():
-    """BASELINE config 4 at full size: 4096^3, m * 2^e entries (seed 4), k = 8,
+    """Benchmark case 4 at full size: 4096^3, m * 2^e entries (seed 4), k = 8,
     against fp64 BLAS (cuBLAS DGEMM) on the same inputs."""
     rng = np.random.default_rng(4)
     A = rng.standard_normal((4096, 4096)) * np.exp2(rng.integers(-10, 11, (4096, 4096)))

@@ -1,5 +1,5 @@
 """Fused DF-MP2 pair energy against the fp64 oracle (the reference's chunked
-torch energy on fp64 casts): gate relative error <= 1e-9 (BASELINE: "within
+torch energy on fp64 casts): gate relative error <= 1e-9 (target: "within
 1e-9 Eh", read as relative to the fp64 oracle, since the reference's own fp32
 path is 5.3e-8 off at config 3)."""
 
@@ -51,7 +51,7 @@ def test_pair_ranges_vs_oracle():
 
 
 def test_config3_energy_and_determinism():
-    """BASELINE config 3 (48/432/1152, seed 3) against the reference's fp64 energy."""
+    """Benchmark case 3 (48/432/1152, seed 3) against the reference's fp64 energy."""
     B, eo, ev = _dev(*PE.make_inputs(48, 432, 1152, 3))
     ref = float(ZE["cfg3_E64"])
     E1 = float(energy.batched_pair_energy(B, eo, ev))

@@ -14,7 +14,10 @@
 // zero beyond K; exponents as int32. Float inputs are widened exactly.
 #pragma once
 
+#include <algorithm>
+
 #include "common.cuh"
+#include "runtime.hpp"
 
 namespace tb {
 
@@ -262,99 +265,169 @@ __host__ __device__ __forceinline__ long long blocked_chunk(long long slab, long
 // second copy with another row block (digits2, rb_log2_2; NULL for none).
 // Padded row p maps to logical row (p / gp) * g + p % gp when p % gp < g (else
 // the row is zero padding): the pair energy pads each occupied orbital's nvir
-// rows to a multiple of 128, the GEMM pads the end. A block covers 32 padded
-// rows and kOzSlabs K slabs of 32: every input value of the block is loaded
-// into registers first (sixteen loads in flight a thread), then each slab's
-// digits are staged in shared memory and written 16 bytes at a time.
-constexpr int kOzSlabs = 4;
+// rows to a multiple of 128, the GEMM pads the end. Work unit: a tile of 32
+// padded rows x one 32-wide K slab. The grid is persistent (grid-strided over
+// the tiles); each block keeps kOzBuf - 1 input tiles in flight with
+// element-wise cp.async into a shared-memory ring (zero-fill for padding rows
+// and K >= K_logical), so the loads of later tiles overlap the work on the
+// current one. Each thread then takes 4 consecutive K of one row, packs their
+// 4 digits of each plane into one 32-bit word and stores it straight into the
+// blocked layout (planes RB * 32 bytes apart; a warp's store covers two
+// contiguous 64-byte runs).
+constexpr int kOzBuf = 4;
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async_zfill(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "n"(BYTES), "r"(valid ? BYTES : 0)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 template <typename T>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256)
     ozk_digits_tiled_kernel(const T* __restrict__ X, long long rs, long long ks, int K,
                             long long g, long long gp, long long rows_pad, int kpad, int slices,
                             const int* __restrict__ exps, const int* __restrict__ shift_range,
                             int8_t* __restrict__ digits, int rb_log2,
                             int8_t* __restrict__ digits2, int rb_log2_2) {
-  __shared__ double tile[32][33];
-  __shared__ __align__(16) int8_t dg[12][32][32];
-  const int kb = blockIdx.x * (32 * kOzSlabs);
-  const long long p0 = static_cast<long long>(blockIdx.y) * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  auto src_row = [&](long long p) -> long long {
-    const long long q = p / gp, a = p - q * gp;
-    return (a < g) ? q * g + a : -1;
-  };
-  // scale exponents of this thread's compute rows ty + 8 j: one power-of-two
-  // step (h1 = shift, h2 = 0), or two when the operand needs them
+  __shared__ __align__(16) T tile[kOzBuf][32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y, t = ty * 32 + tx;
+  const int nslab = kpad / 32;
+  const long long nrb = rows_pad / 32;
   const bool two = shift_range[0] > 1023 || shift_range[1] < -1022;
-  int h1[4], h2[4];
+  // Tile cursors (row block, K slab) advance by the grid size without a
+  // division per tile.
+  const long long G = gridDim.x;
+  const long long Gq = G / nslab;
+  const int Gr = static_cast<int>(G - Gq * nslab);
+  struct Cur {
+    long long rb;
+    int slab;
+  };
+  auto advance = [&](Cur& c) {
+    c.rb += Gq;
+    c.slab += Gr;
+    if (c.slab >= nslab) {
+      c.slab -= nslab;
+      ++c.rb;
+    }
+  };
+  // Source row of padded row p0 + i (p0 = 32 * rb; rows_pad < 2^31): one
+  // 32-bit division for p0, then a short carry loop (1 <= g <= gp).
+  const unsigned ug = static_cast<unsigned>(g), ugp = static_cast<unsigned>(gp);
+  auto src_row = [&](unsigned q0, unsigned a0, int i) -> long long {
+    unsigned a = a0 + static_cast<unsigned>(i), q = q0;
+    while (a >= ugp) {
+      a -= ugp;
+      ++q;
+    }
+    return a < ug ? static_cast<long long>(q) * g + a : -1;
+  };
+  // Start the copies of tile c into ring slot `buf` (one commit group per
+  // call, empty past the last tile, so group counting stays uniform).
+  auto issue = [&](const Cur& c, int buf) {
+    if (c.rb < nrb) {
+      const unsigned p0 = static_cast<unsigned>(c.rb * 32);
+      const unsigned q0 = p0 / ugp, a0 = p0 - q0 * ugp;
+      const int k0 = c.slab * 32;
+      if (ks == 1) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const long long r = src_row(p0 + ty + 8 * j);
-    const int shift = r >= 0 ? 6 - exps[r] : 0;
-    h1[j] = two ? ((shift >= 0) ? shift / 2 : -((-shift + 1) / 2)) : shift;
-    h2[j] = shift - h1[j];
-  }
-  T vals[kOzSlabs][4];
-  if (ks == 1) {
-    // thread (tx, ty) loads and converts (row ty + 8 j, k tx) of each slab
+        for (int j = 0; j < 4; ++j) {
+          const int i = ty + 8 * j;
+          const long long r = src_row(q0, a0, i);
+          const int k = k0 + tx;
+          const bool ok = r >= 0 && k < K;
+          cp_async_zfill<sizeof(T)>(&tile[buf][i][tx], ok ? X + r * rs + k : X, ok);
+        }
+      } else {
+        const long long r = src_row(q0, a0, tx);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const long long r = src_row(p0 + ty + 8 * j);
-      const T* xr = X + (r >= 0 ? r : 0) * rs;
-#pragma unroll
-      for (int s = 0; s < kOzSlabs; ++s) {
-        const int k = kb + 32 * s + tx;
-        vals[s][j] = (r >= 0 && k < K) ? __ldg(xr + k) : T(0);
+        for (int j = 0; j < 4; ++j) {
+          const int kk = ty + 8 * j;
+          const int k = k0 + kk;
+          const bool ok = r >= 0 && k < K;
+          cp_async_zfill<sizeof(T)>(&tile[buf][tx][kk],
+                                    ok ? X + r * rs + static_cast<long long>(k) * ks : X, ok);
+        }
       }
     }
-  } else {
-    // thread (tx, ty) loads (row tx, k ty + 8 j): consecutive rows per warp
-    const long long r = src_row(p0 + tx);
-    const T* xr = X + (r >= 0 ? r : 0) * rs;
+    cp_async_commit();
+  };
+  // compute role of this thread: row `crow`, K offsets kq .. kq + 3 of the slab
+  const int crow = t >> 3, kq = (t & 7) * 4;
+  const long long pstride = 32ll << rb_log2, pstride2 = 32ll << rb_log2_2;
+  Cur cc{static_cast<long long>(blockIdx.x) / nslab, static_cast<int>(blockIdx.x % nslab)};
+  Cur cl = cc;
 #pragma unroll
-    for (int s = 0; s < kOzSlabs; ++s)
+  for (int b = 0; b < kOzBuf - 1; ++b) {
+    issue(cl, b);
+    advance(cl);
+  }
+  for (int it = 0; cc.rb < nrb; advance(cc), ++it) {
+    cp_async_wait<kOzBuf - 2>();  // this thread's copies of tile `it` have landed
+    __syncthreads();              // ... everyone's; and slot (it - 1) % kOzBuf is free
+    issue(cl, (it + kOzBuf - 1) % kOzBuf);
+    advance(cl);
+    const int buf = it % kOzBuf;
+    const unsigned p0 = static_cast<unsigned>(cc.rb * 32);
+    const unsigned q0 = p0 / ugp, a0 = p0 - q0 * ugp;
+    const int k0 = cc.slab * 32;
+    const long long r = src_row(q0, a0, crow);
+    const int shift = r >= 0 ? 6 - __ldg(exps + r) : 0;
+    const int h1 = two ? ((shift >= 0) ? shift / 2 : -((-shift + 1) / 2)) : shift;
+    const double f1 = pow2d(h1), f2 = pow2d(shift - h1);
+    double u[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int k = kb + 32 * s + ty + 8 * j;
-        vals[s][j] = (r >= 0 && k < K) ? __ldg(xr + static_cast<long long>(k) * ks) : T(0);
+    for (int e = 0; e < 4; ++e) u[e] = (static_cast<double>(tile[buf][crow][kq + e]) * f1) * f2;
+    int8_t* out = digits + blocked_offset(p0 + crow, k0 + kq, 0, slices, rows_pad, rb_log2);
+    int8_t* out2 = digits2 ? digits2 + blocked_offset(p0 + crow, k0 + kq, 0, slices, rows_pad,
+                                                      rb_log2_2)
+                           : nullptr;
+    // digits of the 4 values, slice by slice (the rounding of oz_digit_loop)
+#pragma unroll
+    for (int sl = 0; sl < 12; ++sl) {
+      if (sl >= slices) break;
+      const double m =
+          __longlong_as_double((static_cast<long long>(1075 - 7 * sl) << 52) | (1ll << 51));
+      int d[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const double s1 = __dadd_rn(u[e], m);
+        d[e] = __double2loint(s1);
+        u[e] = __dsub_rn(u[e], __dsub_rn(s1, m));
       }
+      const uint32_t w = __byte_perm(__byte_perm(d[0], d[1], 0x0040),
+                                     __byte_perm(d[2], d[3], 0x0040), 0x5410);
+      *reinterpret_cast<uint32_t*>(out + sl * pstride) = w;
+      if (out2) *reinterpret_cast<uint32_t*>(out2 + sl * pstride2) = w;
+    }
   }
-  const int t = ty * 32 + tx;
-#pragma unroll
-  for (int s = 0; s < kOzSlabs; ++s) {
-    const int k0 = kb + 32 * s;
-    if (k0 >= kpad) break;  // uniform over the block
-    double v[4];
-    if (ks == 1) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = static_cast<double>(vals[s][j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) tile[tx][ty + 8 * j] = static_cast<double>(vals[s][j]);
-      __syncthreads();
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = tile[ty + 8 * j][tx];
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = ty + 8 * j;
-      oz_digit_loop((v[j] * pow2d(h1[j])) * pow2d(h2[j]), slices,
-                    [&](int sl, int8_t d) { dg[sl][i][tx] = d; });
-    }
-    __syncthreads();
-    // 16-byte stores: (plane, row, K half) items
-    for (int it = t; it < slices * 64; it += 256) {
-      const int sl = it >> 6, row = (it >> 1) & 31, half = it & 1;
-      const uint4 w = *reinterpret_cast<const uint4*>(&dg[sl][row][16 * half]);
-      *reinterpret_cast<uint4*>(digits + blocked_offset(p0 + row, k0 + 16 * half, sl, slices,
-                                                        rows_pad, rb_log2)) = w;
-      if (digits2)
-        *reinterpret_cast<uint4*>(digits2 + blocked_offset(p0 + row, k0 + 16 * half, sl, slices,
-                                                           rows_pad, rb_log2_2)) = w;
-    }
-    __syncthreads();  // dg and tile are rewritten by the next slab
+  cp_async_wait<0>();
+}
+
+// Resident blocks per SM of the digit kernel (its persistent grid size per
+// SM), from the occupancy calculator; cached per element type.
+template <typename T>
+inline int oz_digit_blocks_per_sm() {
+  static int cached = 0;
+  if (cached == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, ozk_digits_tiled_kernel<T>, 256, 0) !=
+            cudaSuccess ||
+        n < 1)
+      n = 1;
+    cached = n;
   }
+  return cached;
 }
 
 // Row max |x| of X (R x K, strides rs, ks) into maxbits (zeroed first).
@@ -386,6 +459,7 @@ inline cudaError_t launch_split_tiled(const T* X, long long rs, long long ks, in
                                       cudaStream_t stream) {
   auto bad_rb = [&](int lg) { return lg < 5 || lg > 7 || (rows_pad & ((1ll << lg) - 1)); };
   if ((R + 31) / 32 > 65535 || rows_pad / 32 > 65535 || (rows_pad & 31) || (kpad & 31) ||
+      g < 1 || gp < g ||
       slices > 12 || bad_rb(rb_log2) || (digits2 && bad_rb(rb_log2_2)))
     return cudaErrorInvalidConfiguration;
   ozk_init_kernel<<<(R + 255) / 256 + 1, 256, 0, stream>>>(scratch.maxbits, R,
@@ -394,9 +468,11 @@ inline cudaError_t launch_split_tiled(const T* X, long long rs, long long ks, in
   launch_rowmax(X, rs, ks, R, K, scratch.maxbits, stream);
   ozk_exps_kernel<<<(R + 255) / 256, 256, 0, stream>>>(scratch.maxbits, R, exps,
                                                        scratch.shift_range);
-  dim3 g3(static_cast<unsigned>((kpad + 32 * kOzSlabs - 1) / (32 * kOzSlabs)),
-          static_cast<unsigned>(rows_pad / 32));
-  ozk_digits_tiled_kernel<T><<<g3, blk, 0, stream>>>(X, rs, ks, K, g, gp, rows_pad, kpad, slices,
+  const long long tiles = (rows_pad / 32) * (kpad / 32);
+  const long long g3 = std::min<long long>(tiles, static_cast<long long>(num_sms()) *
+                                                      oz_digit_blocks_per_sm<T>());
+  if (g3 > 0)
+    ozk_digits_tiled_kernel<T><<<static_cast<unsigned>(g3), blk, 0, stream>>>(X, rs, ks, K, g, gp, rows_pad, kpad, slices,
                                                      exps, scratch.shift_range, digits, rb_log2,
                                                      digits2, rb_log2_2);
   return cudaGetLastError();

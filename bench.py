@@ -6,7 +6,8 @@ the 2-D output-block sharded GEMM C = A @ B, M = N = K = 32768, bf16
 value = whole-job TFLOP/s. The same line carries the DF-MP2 pair-energy step
 of config 5 (nocc 96, nvir 2208, naux 6912, pairs sharded over ranks) in ms.
 Other workloads (--workload): gemm_fp32 (config 5a fp32), gemm8192_bf16 /
-gemm8192_fp32 (single-GPU 8192^3), batched (config 2a), syrk (config 2b),
+gemm8192_fp32 (single-GPU 8192^3), gemm1024 (config 1: fp32 1024^3, transA,
+beta 0.5), batched / batched_bf16 (config 2a), syrk / syrk_bf16 (config 2b),
 gemm_fp64 (config 4), pair3 (config 3), pair5 (config 5b alone), pair5x4
 (config 5b per-pair shape at nocc 4, a small case for profiling), dfmp2 (the
 whole DF-MP2 energy, `parallel.df_mp2_energy`, at the reference's largest
@@ -16,9 +17,11 @@ benchmark shape nbasis/nocc/naux = 768/96/2304).
     torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
 
 Inputs are seeded synthetic tensors with the benchmark cases' shapes and
-distributions, generated on the device (inputs far larger than L2, so no L2
-flush is needed between steps). Timing: CUDA events on the launching stream,
-barrier + synchronize around the K timed steps, max over ranks.
+distributions, generated on the device. Workloads whose operands are larger
+than L2 run back to back; those that fit in L2 (gemm1024, batched_bf16, syrk,
+syrk_bf16) overwrite a 256 MB buffer before every timed step, outside that
+step's events. Timing: CUDA events on the launching stream, barrier +
+synchronize around the K timed steps, max over ranks.
 
 `--impl reference` times the reference's CPU path (its torch/CPU route,
 restated in `oracle/`) on the host cores, rank 0 only, on a bounded sample of
@@ -183,6 +186,40 @@ def timed_steps(step, steps, warmup, world, gpu):
     return max_over_ranks(ms, world), cs.summary()
 
 
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
+
+
+def timed_steps_flushed(step, steps, warmup, world, gpu):
+    """timed_steps for workloads whose operands fit in L2: before every step
+    a 256 MB buffer is overwritten (outside the timed events), and each step
+    is bracketed by its own CUDA events on the launching stream; the mean
+    step time, max over ranks."""
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    with ClockSampler(gpu) as cs:
+        for a, b in ev:
+            flush.fill_(1)
+            a.record()
+            step()
+            b.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    del flush
+    return max_over_ranks(ms, world), cs.summary()
+
+
+# single-GPU workloads whose operands fit in L2 (timed with a flush between steps)
+FLUSHED = ("syrk", "syrk_bf16", "batched_bf16", "gemm1024")
+
+
 def kernel_avg_ms(events):
     torch.cuda.synchronize()
     return sum(a.elapsed_time(b) for a, b in events) / max(len(events), 1)
@@ -229,15 +266,18 @@ def cpu_gemm_sample(n: int, dtype: torch.dtype, budget_s: float = 12.0):
 
 def cpu_single_sample(wl: str, budget_s: float = 10.0):
     """TFLOP/s of the reference's host route (torch on the CPU, all threads)
-    for a single-GPU workload, on a bounded sample: config 2a batched fp32
-    (a subset of the 64 batch entries), config 2b syrk (A @ A^T on a row
-    sample, lower-triangle flops), config 4 gemm_fp64 (fp64 matmul on a row
-    sample: the reference's CPU gemm_fp64 is host BLAS), 8192^3 bf16/fp32."""
+    for a single-GPU workload, on a bounded sample: config 2a batched fp32 /
+    bf16 (a subset of the 64 batch entries), config 2b syrk fp32 / bf16
+    (A @ A^T on a row sample, lower-triangle flops), config 1 (whole 1024^3
+    products, repeated), config 4 gemm_fp64 (fp64 matmul on a row sample: the
+    reference's CPU gemm_fp64 is host BLAS), 8192^3 bf16/fp32."""
     threads = torch.get_num_threads()
     g = torch.Generator().manual_seed(7)
-    if wl == "batched":
-        A = torch.randn(64, 512, 512, generator=g)
-        B = torch.randn(64, 512, 512, generator=g)
+    ldt = torch.bfloat16 if wl.endswith("bf16") else torch.float32
+    lname = str(ldt).split(".")[-1]
+    if wl in ("batched", "batched_bf16"):
+        A = torch.randn(64, 512, 512, generator=g).to(ldt)
+        B = torch.randn(64, 512, 512, generator=g).to(ldt)
         torch.matmul(A[:2], B[:2])
         t0, nb = time.perf_counter(), 0
         while time.perf_counter() - t0 < budget_s / 2 and nb < 64:
@@ -245,19 +285,37 @@ def cpu_single_sample(wl: str, budget_s: float = 10.0):
             nb += 8
         dt = time.perf_counter() - t0
         return {"value": round(nb * 2.0 * 512 ** 3 / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
-                "kind": "port", "sample": f"{nb} of 64 batch entries, torch CPU bmm fp32 (the reference's host route)"}
-    if wl == "syrk":
+                "kind": "port", "sample": f"{nb} of 64 batch entries, torch CPU bmm {lname} (the reference's host route)"}
+    if wl in ("syrk", "syrk_bf16"):
         n = 4096
-        A = torch.randn(n, n, generator=g) / 64
-        rows = 512
-        torch.matmul(A[:64], A.T)
+        A = (torch.randn(n, n, generator=g) / 64).to(ldt)
+        rows = 64
+        torch.matmul(A[:16], A.T)
+        t0 = time.perf_counter()
+        torch.matmul(A[:rows], A.T)
+        per_row = max((time.perf_counter() - t0) / rows, 1e-7)
+        rows = int(max(64, min(n, budget_s / 2 / per_row)))
         t0 = time.perf_counter()
         torch.matmul(A[:rows], A.T)
         dt = time.perf_counter() - t0
         # the reference computes the full square then symmetrises: time per full product
         full_s = dt * n / rows
         return {"value": round(n * (n + 1) * n / full_s / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
-                "kind": "port", "sample": f"{rows} of {n} rows of A @ A^T (torch CPU fp32, the reference's full-square route), lower-triangle flops"}
+                "kind": "port", "sample": f"{rows} of {n} rows of A @ A^T (torch CPU {lname}, the reference's full-square route), lower-triangle flops"}
+    if wl == "gemm1024":
+        n = 1024
+        A = 2 * torch.rand(n, n, generator=g) - 1
+        B = 2 * torch.rand(n, n, generator=g) - 1
+        C = 2 * torch.rand(n, n, generator=g) - 1
+        step = lambda: torch.addmm(C, A.T, B, beta=0.5, alpha=1.0)  # noqa: E731
+        step()
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < budget_s / 4 and reps < 2000:
+            step()
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        return {"value": round(2.0 * n ** 3 / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{reps} whole config-1 products (fp32 1024^3, transA, beta 0.5), torch CPU addmm (the reference's host route)"}
     dt_, n = (torch.float64, 4096) if wl == "gemm_fp64" else ((torch.bfloat16 if wl.endswith("bf16") else torch.float32), 8192)
     v, th, sample = cpu_gemm_sample(n, dt_, budget_s=budget_s)
     return {"value": round(v, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
@@ -503,7 +561,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="spmd",
                     choices=["spmd", "gemm_fp32", "gemm8192_bf16", "gemm8192_fp32", "pair3", "pair5",
-                             "pair5x4", "dfmp2", "gemm_fp64", "batched", "syrk"])
+                             "pair5x4", "dfmp2", "gemm_fp64", "batched", "syrk", "batched_bf16",
+                             "syrk_bf16", "gemm1024"])
     ap.add_argument("--no-pair", action="store_true", help="skip the pair-energy block of the default line")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -679,16 +738,25 @@ def run_single(args, rank, world, gpu):
         B = torch.randn(n, n, device="cuda", generator=g).to(dt)
         fn = lambda: tb.gemm(1.0, A, B)  # noqa: E731
         flops = 2.0 * n ** 3
-    elif wl == "batched":
-        A = torch.randn(64, 512, 512, device="cuda", generator=g)
-        B = torch.randn(64, 512, 512, device="cuda", generator=g)
+    elif wl in ("batched", "batched_bf16"):
+        dt = torch.bfloat16 if wl.endswith("bf16") else torch.float32
+        A = torch.randn(64, 512, 512, device="cuda", generator=g).to(dt)
+        B = torch.randn(64, 512, 512, device="cuda", generator=g).to(dt)
         fn = lambda: tb.batched_gemm(1.0, A, B)  # noqa: E731
         flops = 64 * 2.0 * 512 ** 3
-    elif wl == "syrk":
-        A = torch.randn(4096, 4096, device="cuda", generator=g) / 64
+    elif wl in ("syrk", "syrk_bf16"):
+        dt = torch.bfloat16 if wl.endswith("bf16") else torch.float32
+        A = (torch.randn(4096, 4096, device="cuda", generator=g) / 64).to(dt)
         B = None
         fn = lambda: tb.syrk(1.0, A, uplo="lower")  # noqa: E731
         flops = 4096 * 4097 * 4096.0
+    elif wl == "gemm1024":  # config 1: A stored K x M, transA, beta 0.5
+        n = 1024
+        A = 2 * torch.rand(n, n, device="cuda", generator=g) - 1
+        B = 2 * torch.rand(n, n, device="cuda", generator=g) - 1
+        C = 2 * torch.rand(n, n, device="cuda", generator=g) - 1
+        fn = lambda: tb.gemm(1.0, A, B, 0.5, C, transA=True)  # noqa: E731
+        flops = 2.0 * n ** 3
     else:  # gemm_fp64, config 4
         n = 4096
         A = torch.randn(n, n, device="cuda", dtype=torch.float64, generator=g) * torch.exp2(
@@ -698,22 +766,29 @@ def run_single(args, rank, world, gpu):
         fn = lambda: tb.gemm_fp64(A, B)  # noqa: E731
         flops = 2.0 * n ** 3
     N.launch_count = 0
-    ms, clocks = timed_steps(fn, args.steps, args.warmup, world, gpu)
+    timer = timed_steps_flushed if wl in FLUSHED else timed_steps
+    ms, clocks = timer(fn, args.steps, args.warmup, world, gpu)
     launches = N.launch_count // (args.steps + args.warmup) * args.steps
     value = flops / (ms / 1e3) / 1e12 * world
     line = {"metric": f"{wl} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": str(A.dtype).split(".")[-1],
-            "data": "synthetic (seeded, device generator)", "config": {"workload": wl, "replicas": world},
+            "data": "synthetic (seeded, device generator)",
+            "config": {"workload": wl, "replicas": world,
+                       "l2": "256 MB flush before each timed step" if wl in FLUSHED else "operands larger than L2"},
             "clocks": clocks, "gpu_launches": launches}
-    line["roofline"] = single_roofline(wl, A, B, flops)
+    line["roofline"] = single_roofline(wl, A, B, flops, C if wl == "gemm1024" else None)
     # e2e: the same public call on pinned host operands, result back on the host
     Ah = A.cpu().pin_memory()
     Bh = B.cpu().pin_memory() if B is not None else None
+    Ch = C.cpu().pin_memory() if wl == "gemm1024" else None
     host_fn = {
         "gemm_fp64": lambda: tb.gemm_fp64(Ah, Bh),
         "batched": lambda: tb.batched_gemm(1.0, Ah, Bh),
+        "batched_bf16": lambda: tb.batched_gemm(1.0, Ah, Bh),
         "syrk": lambda: tb.syrk(1.0, Ah, uplo="lower"),
+        "syrk_bf16": lambda: tb.syrk(1.0, Ah, uplo="lower"),
+        "gemm1024": lambda: tb.gemm(1.0, Ah, Bh, 0.5, Ch, transA=True),
     }.get(wl, lambda: tb.gemm(1.0, Ah, Bh))
     res = {}
 
@@ -725,7 +800,8 @@ def run_single(args, rank, world, gpu):
     out_bytes = res["r"].numel() * res["r"].element_size()
     line["e2e"] = {"value": round(flops / (e2e_ms / 1e3) / 1e12 * world, 2), "unit": "TFLOP/s",
                    "ms_per_step": round(e2e_ms, 4),
-                   "h2d_bytes_per_step": int((Ah.numel() + (Bh.numel() if Bh is not None else 0)) * Ah.element_size() * world),
+                   "h2d_bytes_per_step": int((Ah.numel() + (Bh.numel() if Bh is not None else 0)
+                                              + (Ch.numel() if Ch is not None else 0)) * Ah.element_size() * world),
                    "d2h_bytes_per_step": int(out_bytes * world),
                    "path": "the same public call on pinned host operands"}
     if rank == 0 and world == 1:
@@ -733,11 +809,14 @@ def run_single(args, rank, world, gpu):
     return line
 
 
-def single_roofline(wl, A, B, flops):
+def single_roofline(wl, A, B, flops, C=None):
     """Roofline of the library call alone (device time between CUDA events on
-    the launching stream, no host checks): gemm_fp64 against the int8 tensor
+    the launching stream, no host checks; an L2 flush before each call for the
+    workloads whose operands fit in L2): gemm_fp64 against the int8 tensor
     pipe (k (k + 1) / 2 int8 slice products, the split included in the time),
-    the others against the bf16 / 3xTF32 tensor rate."""
+    bf16 batched against HBM (its operands and result: 100.7 MB a call; the
+    MMA work needs 7.6 us at the bf16 peak), the others against the bf16 /
+    3xTF32 tensor rate."""
     import trnblas_b200 as tb
     from trnblas_b200 import level3
 
@@ -747,7 +826,9 @@ def single_roofline(wl, A, B, flops):
         call = lambda: level3._gemm_fp64_device(A, B, k)  # noqa: E731
     elif wl.startswith("gemm8192"):
         call = lambda: tb.gemm(1.0, A, B)  # noqa: E731
-    elif wl == "batched":
+    elif wl == "gemm1024":
+        call = lambda: tb.gemm(1.0, A, B, 0.5, C, transA=True)  # noqa: E731
+    elif wl.startswith("batched"):
         call = lambda: tb.batched_gemm(1.0, A, B)  # noqa: E731
     else:
         call = lambda: tb.syrk(1.0, A, uplo="lower")  # noqa: E731
@@ -756,12 +837,24 @@ def single_roofline(wl, A, B, flops):
     reps = 5
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    s.record()
-    for _ in range(reps):
-        call()
-    e.record()
-    torch.cuda.synchronize()
-    kms = s.elapsed_time(e) / reps
+    if wl in FLUSHED:
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in ev:
+            flush.fill_(1)
+            a.record()
+            call()
+            b.record()
+        torch.cuda.synchronize()
+        kms = sum(a.elapsed_time(b) for a, b in ev) / reps
+        del flush
+    else:
+        s.record()
+        for _ in range(reps):
+            call()
+        e.record()
+        torch.cuda.synchronize()
+        kms = s.elapsed_time(e) / reps
     if wl == "gemm_fp64":
         M, K = A.shape
         ops = k * (k + 1) / 2 * 2.0 * M * B.shape[1] * K
@@ -783,6 +876,13 @@ def single_roofline(wl, A, B, flops):
                 "cublas_dgemm_tflops": round(dgemm, 2),
                 "peak_source": f"{src}: 2 x bf16 burst (int8 dense rate = 2 x bf16), int8 ops"}
     bf16 = A.dtype == torch.bfloat16
+    if wl == "batched_bf16":
+        nbytes = 3.0 * A.numel() * A.element_size()  # A, B read; C written
+        gbs = nbytes / (kms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": read_traffic("gemm_batched_bf16"),
+                "kernel_ms": round(kms, 4), "algorithmic_bytes": int(nbytes),
+                "peak_source": f"{src} HBM copy bandwidth"}
     peak = pk["bf16_tflops"] if bf16 else pk["bf16_tflops"] / 6.0
     achieved = flops / (kms / 1e3) / 1e12
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
@@ -810,7 +910,7 @@ def reference_arm(args, world):
                 "steps": 1, "warmup": 1, "config": {"workload": args.workload},
                 "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample},
                 "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    if args.workload in ("batched", "syrk", "gemm_fp64"):
+    if args.workload in ("batched", "syrk", "gemm_fp64", "batched_bf16", "syrk_bf16", "gemm1024"):
         cb = cpu_single_sample(args.workload, budget_s=8.0)
         return {"impl": "reference", "metric": f"{args.workload} TFLOP/s", "value": cb["value"], "unit": "TFLOP/s",
                 "higher_is_better": True, "n_gpus": world, "steps": 1, "warmup": 1,

@@ -206,6 +206,51 @@ __device__ __forceinline__ void store_d(void* D, int out_kind, long long idx, fl
   }
 }
 
+// Store out[0..31] at D[row offset drow + c0 ..]: 16-byte vector stores when
+// all 32 columns exist and the row start is 16-byte aligned, else element by
+// element up to column N.
+__device__ __forceinline__ void store_row32(const GemmParams& p, long long drow, int c0,
+                                            const float* out, bool full) {
+  if (p.out_kind == kOutF32) {
+    float* dp = reinterpret_cast<float*>(p.D) + drow + c0;
+    if (full && (p.ldd % 4 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
+      float4* d4 = reinterpret_cast<float4*>(dp);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        d4[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < p.N) dp[j] = out[j];
+    }
+  } else {
+    unsigned short* dp = reinterpret_cast<unsigned short*>(p.D) + drow + c0;
+    if (full && (p.ldd % 8 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
+      uint4* d4 = reinterpret_cast<uint4*>(dp);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float lo = out[8 * j + 2 * h], hi = out[8 * j + 2 * h + 1];
+          if (p.out_kind == kOutBF16) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+            w[h] = *reinterpret_cast<uint32_t*>(&b2);
+          } else {
+            __half2 h2 = __floats2half2_rn(lo, hi);
+            w[h] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+        d4[j] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < p.N) store_d(p.D, p.out_kind, drow + c0 + j, out[j]);
+    }
+  }
+}
+
 // Epilogue for one 32-column chunk held by this thread: row r (global), columns
 // c0 .. c0+31 (global), accumulator values v[0..31].
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int r, int c0,
@@ -239,49 +284,25 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int 
           if (c0 + j < p.N) out[j] += p.beta * load_c(p.C, p.out_kind, crow + c0 + j);
       }
     }
-    const long long drow = dbase + static_cast<long long>(r) * p.ldd;
-    if (p.out_kind == kOutF32) {
-      float* dp = reinterpret_cast<float*>(p.D) + drow + c0;
-      if (full && (p.ldd % 4 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
-        float4* d4 = reinterpret_cast<float4*>(dp);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          d4[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < p.N) dp[j] = out[j];
-      }
-    } else {
-      unsigned short* dp = reinterpret_cast<unsigned short*>(p.D) + drow + c0;
-      if (full && (p.ldd % 8 == 0) && ((reinterpret_cast<uintptr_t>(dp) & 15) == 0)) {
-        uint4* d4 = reinterpret_cast<uint4*>(dp);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t w[4];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float lo = out[8 * j + 2 * h], hi = out[8 * j + 2 * h + 1];
-            if (p.out_kind == kOutBF16) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
-              w[h] = *reinterpret_cast<uint32_t*>(&b2);
-            } else {
-              __half2 h2 = __floats2half2_rn(lo, hi);
-              w[h] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-          }
-          d4[j] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < p.N) store_d(p.D, p.out_kind, drow + c0 + j, out[j]);
-      }
-    }
+    store_row32(p, dbase + static_cast<long long>(r) * p.ldd, c0, out, full);
     return;
   }
   // SYRK: lower element (r, c) with r >= c, mirrored to (c, r).
   const int n = p.M;
+  if (!diag_tile && !has_c && r < n && c0 + 32 <= n) {
+    // off-diagonal chunk: the row r part as the GEMM writes it (vector
+    // stores along the row; the lanes hold 32 different rows), the mirror
+    // (c, r) element by element (the lanes' consecutive r: one contiguous
+    // run per column)
+    float out[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
+    store_row32(p, dbase + static_cast<long long>(r) * p.ldd, c0, out, true);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      store_d(p.D, p.out_kind, dbase + static_cast<long long>(c0 + j) * p.ldd + r, out[j]);
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const int c = c0 + j;

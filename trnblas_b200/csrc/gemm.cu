@@ -182,7 +182,7 @@ template <int KIND, int BN, int STAGES>
 int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
                 const CUtensorMap& b1, GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<KIND, BN>;
-  constexpr int smem = STAGES * Cfg::STAGE_BYTES + 1024 + 256;
+  constexpr int smem = STAGES * Cfg::STAGE_BYTES + 1024 + kGemmBarBytes + kEpiStageBytes;
   auto kern = gemm_sm100_kernel<KIND, BN, STAGES>;
   static bool attr_set[64] = {};  // the attribute is set per device
   const int dev = current_device();

@@ -55,6 +55,11 @@ struct GemmParams {
   unsigned long long timeout_ns;
 };
 
+// Shared memory after the pipeline stages: 256 bytes of barriers, then one
+// 4 KB transpose stage per epilogue warp (SYRK mirror stores).
+constexpr int kGemmBarBytes = 256;
+constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;
+
 template <int KIND, int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
@@ -251,10 +256,50 @@ __device__ __forceinline__ void store_row32(const GemmParams& p, long long drow,
   }
 }
 
+// SYRK mirror of one warp's 32 x 32 block: lane l holds out[j] = value at
+// (r0 + l, c0 + j); D(c0 + j, r0 + l) receives it. The block goes through
+// this warp's shared-memory stage `tsm` (row j = mirror row c0 + j, lanes
+// along it: conflict-free) and leaves as 16-byte stores, each warp store
+// covering four whole 128-byte mirror rows, instead of 32 element stores.
+// Needs ldd and the row starts 16-byte aligned (checked by the caller).
+__device__ __forceinline__ void syrk_mirror_block(const GemmParams& p, long long dbase, int r0,
+                                                  int c0, const float* out, void* tsm) {
+  const int lane = threadIdx.x & 31;
+  if (p.out_kind == kOutF32) {
+    float* T = reinterpret_cast<float*>(tsm);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) T[j * 32 + lane] = out[j];
+    __syncwarp();
+    float* D = reinterpret_cast<float*>(p.D) + dbase + r0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = 4 * k + (lane >> 3), q4 = (lane & 7) * 4;
+      *reinterpret_cast<float4*>(D + static_cast<long long>(c0 + row) * p.ldd + q4) =
+          *reinterpret_cast<const float4*>(&T[row * 32 + q4]);
+    }
+  } else {
+    unsigned short* T = reinterpret_cast<unsigned short*>(tsm);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      T[j * 32 + lane] = (p.out_kind == kOutBF16) ? __bfloat16_as_ushort(__float2bfloat16_rn(out[j]))
+                                                  : __half_as_ushort(__float2half_rn(out[j]));
+    __syncwarp();
+    unsigned short* D = reinterpret_cast<unsigned short*>(p.D) + dbase + r0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int row = 8 * k + (lane >> 2), q8 = (lane & 3) * 8;
+      *reinterpret_cast<uint4*>(D + static_cast<long long>(c0 + row) * p.ldd + q8) =
+          *reinterpret_cast<const uint4*>(&T[row * 32 + q8]);
+    }
+  }
+  __syncwarp();  // the stage is rewritten by the next chunk
+}
+
 // Epilogue for one 32-column chunk held by this thread: row r (global), columns
-// c0 .. c0+31 (global), accumulator values v[0..31].
+// c0 .. c0+31 (global), accumulator values v[0..31]. `tsm`: this warp's 4 KB
+// shared-memory stage (SYRK mirror).
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int r, int c0,
-                                               const float* v, bool diag_tile) {
+                                               const float* v, bool diag_tile, void* tsm) {
   const long long dbase = static_cast<long long>(bz) * p.strideD;
   const long long cbase = static_cast<long long>(bz) * p.strideC;
   const bool has_c = (p.c_mode != kCNone) && (p.beta != 0.0f);
@@ -289,18 +334,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int 
   }
   // SYRK: lower element (r, c) with r >= c, mirrored to (c, r).
   const int n = p.M;
-  if (!diag_tile && !has_c && r < n && c0 + 32 <= n) {
-    // off-diagonal chunk: the row r part as the GEMM writes it (vector
-    // stores along the row; the lanes hold 32 different rows), the mirror
-    // (c, r) element by element (the lanes' consecutive r: one contiguous
-    // run per column)
+  const int r0 = r - static_cast<int>(threadIdx.x & 31);  // this warp's first row
+  // whole 32 x 32 block below the diagonal and inside the matrix (uniform
+  // over the warp): the row part as the GEMM writes it, the mirror through
+  // the transpose stage
+  const int vec = (p.out_kind == kOutF32) ? 4 : 8;
+  if (c0 + 31 <= r0 && r0 + 32 <= n && !has_c && p.ldd % vec == 0 &&
+      ((reinterpret_cast<uintptr_t>(p.D) + static_cast<uintptr_t>(dbase) * (p.out_kind == kOutF32 ? 4 : 2)) & 15) == 0) {
     float out[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
     store_row32(p, dbase + static_cast<long long>(r) * p.ldd, c0, out, true);
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      store_d(p.D, p.out_kind, dbase + static_cast<long long>(c0 + j) * p.ldd + r, out[j]);
+    syrk_mirror_block(p, dbase, r0, c0, out, tsm);
     return;
   }
 #pragma unroll
@@ -335,6 +380,7 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  static_assert((2 * STAGES + 2 * Cfg::NBUF + 1) * 8 + 8 <= kGemmBarBytes, "barrier block");
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;   // [NBUF]
@@ -458,6 +504,7 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = 32 * q + lane;
+    void* tsm = smem + STAGES * STAGE_BYTES + kGemmBarBytes + (warp - 2) * (kEpiStageBytes / 4);
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
     int gc = 0;
     bool aborted = false;
@@ -485,7 +532,7 @@ __global__ void __launch_bounds__(192, 1)
             float f[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) f[j] = u2f(v[j]);
-            epilogue_chunk(p, bz, r, n0 + c * 32, f, diag);
+            epilogue_chunk(p, bz, r, n0 + c * 32, f, diag, tsm);
           }
         }
         tc_fence_before();
@@ -519,7 +566,7 @@ __global__ void __launch_bounds__(192, 1)
         if (aborted) break;
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
-          if (n0 + c * 32 < nlim) epilogue_chunk(p, bz, r, n0 + c * 32, sum + c * 32, diag);
+          if (n0 + c * 32 < nlim) epilogue_chunk(p, bz, r, n0 + c * 32, sum + c * 32, diag, tsm);
       }
     }
   }

@@ -162,6 +162,21 @@ def test_syrk_golden_reference_cases():
     assert relf(r, s["lower"]) <= 1e-5
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,k", [(256, 96), (640, 130), (1100, 64), (2176, 200)])
+@pytest.mark.parametrize("trans", [False, True])
+def test_syrk_without_c_every_tile_walk(dt, n, k, trans):
+    """No C: off-diagonal blocks take the vector row stores and the
+    transposed mirror stores; 16-bit types walk 128 x 256 tiles over the
+    lower triangle's column-block pairs (odd and even tile-row counts, a
+    ragged last row block at n = 1100)."""
+    A = (torch.randn(k, n, device=DEV) if trans else torch.randn(n, k, device=DEV)).to(dt)
+    out = tb.syrk(0.75, A, trans=trans, uplo="lower")
+    assert torch.equal(out, out.T)
+    a = A.double().T if trans else A.double()
+    assert relf(out, 0.75 * a @ a.T) <= TOL[dt]
+
+
 def test_syrk_config2_lower():
     """Benchmark case 2b: n = k = 4096, uplo lower, A ~ N(0, 1/k), seed 2."""
     gen = torch.Generator().manual_seed(2)

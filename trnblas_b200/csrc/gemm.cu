@@ -486,10 +486,20 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
     return TRNBLAS_ERR_ARG;
   }
   const long long s2 = round_up(lda * rows, 8);
+  // 128 x 256 tiles over the lower triangle's column-block pairs: half the
+  // operand bytes per MMA of 128 x 128 tiles, and half the tiles
+  CUtensorMap mb0;
   const bool ok = trans ? encode_map_3d(&ma0, dt, 2, A, n, k, 1, lda, s2, 64, 64)
-                        : encode_map_3d(&ma0, dt, 2, A, k, n, 1, lda, s2, 64, 128);
+                        : (encode_map_3d(&ma0, dt, 2, A, k, n, 1, lda, s2, 64, 128) &&
+                           encode_map_3d(&mb0, dt, 2, A, k, n, 1, lda, s2, 64, 256));
   if (!ok) return TRNBLAS_ERR_ALIGN;
-  return launch_gemm<kF16, 128, 6>(ma0, ma0, ma0, ma0, p, stream);
+  if (trans) mb0 = ma0;  // MN-major: 64 x 64 boxes for either operand
+  p.mode = kModeSyrkWide;
+  {
+    const int T = p.tiles_m, h = T >> 1;
+    p.num_tiles = (T & 1) ? (h + 1) * (h + 1) : h * (h + 1);
+  }
+  return launch_gemm<kF16, 256, 4>(ma0, ma0, mb0, mb0, p, stream);
 }
 
 }  // extern "C"

@@ -19,9 +19,10 @@
 // Modes:
 //   GEMM  tiles of D[b] = alpha * op(A[b]) op(B[b]) + beta * C[b], batched
 //         over a grid dimension folded into the tile index;
-//   SYRK  lower-triangle tiles only (BM == BN); each value v(r,c), r >= c, is
-//         stored at (r,c) and mirrored to (c,r), so the full symmetric result
-//         is exactly symmetric and the upper tiles are never computed.
+//   SYRK  lower-triangle tiles only (BM x BM, or BM x 2BM over column-block
+//         pairs); each value v(r,c), r >= c, is stored at (r,c) and mirrored
+//         to (c,r), so the full symmetric result is exactly symmetric and the
+//         upper tiles are never computed.
 #pragma once
 
 #include "common.cuh"
@@ -30,7 +31,11 @@ namespace tb {
 
 enum GemmKind : int { kF16 = 0, kTF32x3 = 1 };
 enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
-enum GemmMode : int { kModeGemm = 0, kModeSyrk = 1 };
+// kModeSyrk: lower-triangle BM x BM tiles; kModeSyrkWide: BM x BN tiles
+// (BN = 2 BM) over the lower triangle's column-block pairs, row m holding
+// pairs 0 .. m / 2 (the last pair of an even row also spans the strictly upper
+// block (m, m + 1), which the epilogue skips).
+enum GemmMode : int { kModeGemm = 0, kModeSyrk = 1, kModeSyrkWide = 2 };
 // How the epilogue reads C: not at all, C[r][c], or (SYRK, upper-triangle
 // storage) C[c][r] for the lower element (r, c).
 enum CMode : int { kCNone = 0, kCRow = 1, kCTrans = 2 };
@@ -178,6 +183,17 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz,
     bz = 0;
     mb = m;
     nb = t - m * (m + 1) / 2;
+    return;
+  }
+  if (p.mode == kModeSyrkWide) {
+    // rows before m hold S(m) tiles: S(2k) = k (k + 1), S(2k + 1) = (k + 1)^2
+    auto S = [](int m) { const int k = m >> 1; return (m & 1) ? (k + 1) * (k + 1) : k * (k + 1); };
+    int m = static_cast<int>(2.0f * sqrtf(static_cast<float>(t)));
+    while (m > 0 && S(m) > t) --m;
+    while (S(m + 1) <= t) ++m;
+    bz = 0;
+    mb = m;
+    nb = t - S(m);
     return;
   }
   const int per_batch = p.tiles_m * p.tiles_n;
@@ -515,7 +531,9 @@ __global__ void __launch_bounds__(192, 1)
       const int ncol = (p.mode == kModeSyrk) ? BM : BN;
       const int n0 = nb * ncol;
       const int nlim = (p.mode == kModeSyrk) ? p.M : p.N;
-      const bool diag = (p.mode == kModeSyrk) && (mb == nb);
+      // a SYRK tile reaching the diagonal takes the masked path per block
+      const bool diag = (p.mode == kModeSyrk && mb == nb) ||
+                        (p.mode == kModeSyrkWide && n0 + BN - 1 > mb * BM);
       if (KIND == kF16) {
         // whole K in one TMEM accumulator
         const int buf = gc % Cfg::NBUF;

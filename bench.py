@@ -107,12 +107,17 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU's SM clock and throttle reasons."""
+    """nvidia-smi samples of this GPU's SM clock and throttle reasons. The
+    sampler is started, and its first sample awaited, before the warm-up steps
+    (so its start-up does not fall inside the timed region); the summary keeps
+    the samples taken between start() and stop() (all of them when the region
+    is shorter than the 200 ms sampling period)."""
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
         self.lines = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -130,7 +135,18 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def ready(self, timeout: float = 5.0):
+        end = time.monotonic() + timeout
+        while self.proc is not None and not self.lines and time.monotonic() < end:
+            time.sleep(0.01)
+
+    def start(self):
+        self.t0 = time.monotonic()
+
+    def stop(self):
+        self.t1 = time.monotonic()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -142,7 +158,11 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        for ln in self.lines:
+        lines = self.lines
+        if self.t0 is not None and self.t1 is not None:
+            inside = [x for x in lines if self.t0 <= x[0] <= self.t1 + 0.25]
+            lines = inside or lines
+        for _, ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 3:
                 continue
@@ -167,12 +187,14 @@ class ClockSampler:
 
 
 def timed_steps(step, steps, warmup, world, gpu):
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(gpu) as cs:
+        cs.ready()
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        cs.start()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
@@ -182,6 +204,7 @@ def timed_steps(step, steps, warmup, world, gpu):
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
+        cs.stop()
     ms = s.elapsed_time(e) / steps
     return max_over_ranks(ms, world), cs.summary()
 
@@ -195,14 +218,16 @@ def timed_steps_flushed(step, steps, warmup, world, gpu):
     is bracketed by its own CUDA events on the launching stream; the mean
     step time, max over ranks."""
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-    for _ in range(warmup):
-        flush.fill_(1)
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     with ClockSampler(gpu) as cs:
+        cs.ready()
+        for _ in range(warmup):
+            flush.fill_(1)
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        cs.start()
         for a, b in ev:
             flush.fill_(1)
             a.record()
@@ -211,6 +236,7 @@ def timed_steps_flushed(step, steps, warmup, world, gpu):
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
+        cs.stop()
     ms = sum(a.elapsed_time(b) for a, b in ev) / steps
     del flush
     return max_over_ranks(ms, world), cs.summary()

@@ -43,6 +43,25 @@ def test_split_bitwise_vs_reference(k):
     assert np.array_equal(d.transpose(0, 2, 1), Z[f"split_col_{k}_d"]) and np.array_equal(e, Z[f"split_col_{k}_e"])
 
 
+@pytest.mark.parametrize("k", [5, 8])
+def test_split_any_strides_bitwise(k):
+    """Element (r, c) at X[r * rs + c * ks] with neither stride 1 (every other
+    column of a wider matrix): the generic row-max pass and the digit pass
+    give the digits of the same matrix made contiguous, bit for bit."""
+    X = Z["X"]
+    R, K = X.shape
+    wide = np.zeros((R, 2 * K))
+    wide[:, ::2] = X
+    Wd = torch.from_numpy(wide).to(DEV)
+    dig = torch.empty((k, R, K), dtype=torch.int8, device=DEV)
+    ex = torch.empty(R, dtype=torch.int32, device=DEV)
+    ws = torch.empty(8 * R + 256, dtype=torch.uint8, device=DEV)
+    N.check(N.lib().trnblas_ozaki_split(R, K, Wd.data_ptr(), 2 * K, 2, k, dig.data_ptr(), K, ex.data_ptr(),
+                                        ws.data_ptr(), ws.numel(), N.stream_ptr(Wd.device)), "split")
+    d, e = _split(X, k)
+    assert np.array_equal(dig.cpu().numpy(), d) and np.array_equal(ex.cpu().numpy().astype(np.int64), e)
+
+
 def test_split_extreme_rows_bitwise():
     d, e = _split(Z["Xe"], 8)
     assert np.array_equal(d, Z["split_extreme_d"]) and np.array_equal(e, Z["split_extreme_e"])

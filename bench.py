@@ -245,6 +245,18 @@ def timed_steps_flushed(step, steps, warmup, world, gpu):
 # single-GPU workloads whose operands fit in L2 (timed with a flush between steps)
 FLUSHED = ("syrk", "syrk_bf16", "batched_bf16", "gemm1024")
 
+# the profiles/ capture whose per-launch DRAM traffic a workload's roofline
+# reports (the dominant kernel of that workload, captured on the same shape)
+TRAFFIC_PROFILE = {
+    "gemm8192_bf16": "gemm_bf16_8192",
+    "gemm8192_fp32": "gemm_fp32_8192",
+    "batched": "gemm_batched_64x512",
+    "batched_bf16": "gemm_batched_bf16",
+    "syrk": "gemm_syrk_4096",
+    "syrk_bf16": "gemm_syrk_bf16_4096",
+    "gemm_fp64": "ozaki_fp64_4096",
+}
+
 
 def kernel_avg_ms(events):
     torch.cuda.synchronize()
@@ -896,7 +908,7 @@ def single_roofline(wl, A, B, flops, C=None):
         torch.cuda.synchronize()
         dgemm = flops / (s.elapsed_time(e) / reps / 1e3) / 1e12
         return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TOP/s (int8)",
-                "frac": round(achieved / peak, 4), "traffic": read_traffic("ozaki_fp64_4096"),
+                "frac": round(achieved / peak, 4), "traffic": read_traffic(TRAFFIC_PROFILE["gemm_fp64"]),
                 "kernel": "ozk split + ozaki_gemm_kernel (one trnblas_gemm_fp64 call)",
                 "kernel_ms": round(kms, 4), "fp64_tflops_of_call": round(flops / (kms / 1e3) / 1e12, 2),
                 "cublas_dgemm_tflops": round(dgemm, 2),
@@ -906,14 +918,14 @@ def single_roofline(wl, A, B, flops, C=None):
         nbytes = 3.0 * A.numel() * A.element_size()  # A, B read; C written
         gbs = nbytes / (kms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": read_traffic("gemm_batched_bf16"),
+                "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": read_traffic(TRAFFIC_PROFILE["batched_bf16"]),
                 "kernel_ms": round(kms, 4), "algorithmic_bytes": int(nbytes),
                 "peak_source": f"{src} HBM copy bandwidth"}
     peak = pk["bf16_tflops"] if bf16 else pk["bf16_tflops"] / 6.0
     achieved = flops / (kms / 1e3) / 1e12
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
-            "traffic": read_traffic("gemm_bf16_8192" if bf16 else "gemm_fp32_8192") if wl.startswith("gemm8192") else None,
+            "traffic": read_traffic(TRAFFIC_PROFILE[wl]) if wl in TRAFFIC_PROFILE else None,
             "kernel_ms": round(kms, 4),
             "peak_source": f"{src} bf16 burst" + ("" if bf16 else " / 6 (3 tf32 products at half the bf16 rate)")}
 

@@ -16,6 +16,14 @@ from .level3 import batched_gemm, gemm, gemm_fp64, metric_inv_half, symm, syrk, 
 
 __version__ = "0.1.0"
 
+__all__ = [
+    "gemm", "batched_gemm", "syrk", "gemm_fp64", "trsm", "metric_inv_half", "symm", "trmm",
+    "batched_pair_energy", "nki_batched_pair_energy", "pair_range_energy",
+    "energy", "parallel",
+    "trans_flag", "uplo_flag", "side_flag", "diag_flag",
+    "set_backend", "get_backend", "device_status",
+]
+
 _BACKENDS = ("auto", "pytorch", "nki", "cuda")
 _backend = "auto"
 

@@ -245,16 +245,19 @@ def timed_steps_flushed(step, steps, warmup, world, gpu):
 # single-GPU workloads whose operands fit in L2 (timed with a flush between steps)
 FLUSHED = ("syrk", "syrk_bf16", "batched_bf16", "gemm1024")
 
-# the profiles/ capture whose per-launch DRAM traffic a workload's roofline
-# reports (the dominant kernel of that workload, captured on the same shape)
-TRAFFIC_PROFILE = {
-    "gemm8192_bf16": "gemm_bf16_8192",
-    "gemm8192_fp32": "gemm_fp32_8192",
-    "batched": "gemm_batched_64x512",
-    "batched_bf16": "gemm_batched_bf16",
-    "syrk": "gemm_syrk_4096",
-    "syrk_bf16": "gemm_syrk_bf16_4096",
-    "gemm_fp64": "ozaki_fp64_4096",
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, one
+# ncu capture of the workload's dominant kernel on the same shape; the
+# summaries with their commands are under profiles/, named in the comments).
+# None where no capture of the timed shape exists.
+TRAFFIC = {
+    "gemm8192_bf16": 1136268400,   # profiles/gemm_bf16_8192.md
+    "gemm8192_fp32": 6728923480,   # profiles/gemm_fp32_8192.md
+    "batched": 313154560,          # profiles/gemm_batched_64x512.md
+    "batched_bf16": 70896640,      # profiles/gemm_batched_bf16.md
+    "syrk": 528911104,             # profiles/gemm_syrk_4096.md
+    "syrk_bf16": 34854912,         # profiles/gemm_syrk_bf16_4096.md
+    "gemm_fp64": 2161969960,       # profiles/ozaki_fp64_4096.md (the int8 GEMM kernel)
+    "pair3": 2699185008,           # profiles/pair_energy_pair3.md
 }
 
 
@@ -263,19 +266,20 @@ def kernel_avg_ms(events):
     return sum(a.elapsed_time(b) for a, b in events) / max(len(events), 1)
 
 
-def read_traffic(name: str):
-    """Per-launch DRAM bytes for a kernel/workload from its ncu summary in
-    profiles/ (a line 'traffic_bytes_per_launch: <int>'), or None."""
-    p = ROOT / "profiles" / f"{name}.md"
-    if not p.exists():
-        return None
-    for ln in p.read_text().splitlines():
-        if ln.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(float(ln.split(":", 1)[1].strip()))
-            except ValueError:
-                return None
-    return None
+# ── metric names (one string per metric, shared by both arms) ───────────────
+
+
+def gemm_metric(n: int, dtype: torch.dtype) -> str:
+    return f"GEMM TFLOP/s (M=N=K={n}, {str(dtype).split('.')[-1]})"
+
+
+def pair_metric(nocc: int, nvir: int, naux: int) -> str:
+    return f"DF-MP2 pair-energy step ms ({nocc}/{nvir}/{naux})"
+
+
+# The pair-energy block of the default line (config 5b): its own step counts,
+# reported in the block (a config-5b step takes seconds on one GPU).
+PAIR5_STEPS, PAIR5_WARMUP = 5, 3
 
 
 # ── CPU baseline (the reference's CPU route, restated) ──────────────────────
@@ -443,7 +447,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
     del Ah, Bh
     es = A_sh.element_size()
     line = {
-        "metric": f"GEMM TFLOP/s (2-D sharded, M=N=K={n}, {str(dtype).split('.')[-1]})",
+        "metric": gemm_metric(n, dtype),
         "value": round(value, 2),
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -470,8 +474,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
             "peak_source": f"{src} {'bf16 sustained' if dtype == torch.bfloat16 else 'bf16 sustained / 6 (3 tf32 products at half the bf16 rate)'}",
             "kernel": "gemm_sm100_kernel",
             "kernel_ms": round(kern_ms, 4),
-            "traffic": read_traffic("gemm_bf16_8192" if dtype == torch.bfloat16 else "gemm_fp32_8192"),
-            "traffic_note": "per launch of the 8192^3 ncu capture (profiles/), not scaled",
+            "traffic": TRAFFIC.get(f"spmd_{'bf16' if dtype == torch.bfloat16 else 'fp32'}_{pr}x{pc}"),
         },
         "e2e": {
             "value": round(flops / (e2e_ms / 1e3) / 1e12, 2),
@@ -605,12 +608,14 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.impl == "reference":
+        # the host cores of rank 0 alone; the other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(reference_arm(args, world)), flush=True)
+        return
     rank, world, local = setup_dist(args.gpus)
     try:
-        if args.impl == "reference":
-            if rank == 0:
-                print(json.dumps(reference_arm(args, world)), flush=True)
-            return
         line = run_ours(args, rank, world, local)
         if rank == 0:
             print(json.dumps(line), flush=True)
@@ -625,8 +630,11 @@ def run_ours(args, rank, world, gpu):
         dt = torch.bfloat16 if args.workload == "spmd" else torch.float32
         line = run_gemm_spmd(args, rank, world, gpu, dt)
         if args.workload == "spmd" and not args.no_pair:
-            line["pair_energy"] = run_pair(args, rank, world, gpu, 96, 2208, 6912, steps=2, warmup=1)
-            line["pair_energy"]["metric"] = "DF-MP2 pair-energy step ms (config 5: 96/2208/6912)"
+            pe = run_pair(args, rank, world, gpu, 96, 2208, 6912,
+                          steps=min(args.steps, PAIR5_STEPS), warmup=PAIR5_WARMUP)
+            line["pair_energy"] = {"metric": pair_metric(96, 2208, 6912), "value": pe["ms_per_step"],
+                                   "unit": "ms", "higher_is_better": False,
+                                   "steps": min(args.steps, PAIR5_STEPS), "warmup": PAIR5_WARMUP, **pe}
         if rank == 0:
             line["cpu_baseline"] = cpu_baseline_gemm(dt) if world == 1 else None
         return line
@@ -636,14 +644,14 @@ def run_ours(args, rank, world, gpu):
         dims = PAIR_DIMS[args.workload]
         r = run_pair(args, rank, world, gpu, *dims)
         line = {
-            "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
+            "metric": pair_metric(*dims),
             "value": r["ms_per_step"], "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 (5 Ozaki slices, exact int32) + fp64 reduction",
             "data": "synthetic (benchmark recipe, device generator)",
             "config": {"workload": args.workload, **r["config"]},
             "roofline": {"bound": "tensor", "achieved": r["int8_tops_achieved"], "peak": r["int8_peak_tops"],
-                         "unit": "TOP/s (int8)", "frac": r["int8_frac"], "traffic": read_traffic(f"pair_energy_{args.workload}")},
+                         "unit": "TOP/s (int8)", "frac": r["int8_frac"], "traffic": TRAFFIC.get(args.workload)},
             "clocks": r["clocks"], "gpu_launches": r["gpu_launches"], "e2e": r["e2e"], "detail": r,
         }
         if rank == 0 and world == 1:
@@ -908,7 +916,7 @@ def single_roofline(wl, A, B, flops, C=None):
         torch.cuda.synchronize()
         dgemm = flops / (s.elapsed_time(e) / reps / 1e3) / 1e12
         return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TOP/s (int8)",
-                "frac": round(achieved / peak, 4), "traffic": read_traffic(TRAFFIC_PROFILE["gemm_fp64"]),
+                "frac": round(achieved / peak, 4), "traffic": TRAFFIC["gemm_fp64"],
                 "kernel": "ozk split + ozaki_gemm_kernel (one trnblas_gemm_fp64 call)",
                 "kernel_ms": round(kms, 4), "fp64_tflops_of_call": round(flops / (kms / 1e3) / 1e12, 2),
                 "cublas_dgemm_tflops": round(dgemm, 2),
@@ -918,55 +926,102 @@ def single_roofline(wl, A, B, flops, C=None):
         nbytes = 3.0 * A.numel() * A.element_size()  # A, B read; C written
         gbs = nbytes / (kms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": read_traffic(TRAFFIC_PROFILE["batched_bf16"]),
+                "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": TRAFFIC["batched_bf16"],
                 "kernel_ms": round(kms, 4), "algorithmic_bytes": int(nbytes),
                 "peak_source": f"{src} HBM copy bandwidth"}
     peak = pk["bf16_tflops"] if bf16 else pk["bf16_tflops"] / 6.0
     achieved = flops / (kms / 1e3) / 1e12
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
-            "traffic": read_traffic(TRAFFIC_PROFILE[wl]) if wl in TRAFFIC_PROFILE else None,
+            "traffic": TRAFFIC.get(wl),
             "kernel_ms": round(kms, 4),
             "peak_source": f"{src} bf16 burst" + ("" if bf16 else " / 6 (3 tf32 products at half the bf16 rate)")}
 
 
+def _ref_line(args, world, metric, unit, hib, value, ms_per_step, cb, extra=None, steps=None, warmup=None):
+    """The reference arm's JSON line: the same metric, unit and direction as
+    this repo's line for the workload, the step counts it ran (the driver's
+    for the default workload) with the wall time of one timed step, and the
+    sample it timed."""
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "higher_is_better": hib,
+            "n_gpus": world, "steps": args.steps if steps is None else steps,
+            "warmup": args.warmup if warmup is None else warmup, "ms_per_step": round(ms_per_step, 3),
+            "config": {"workload": args.workload, "timed": "each step is a bounded sample of the workload on the host cores"},
+            "cpu_baseline": {**cb, "value": value},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if extra:
+        line.update(extra)
+    return line
+
+
+def _ref_steps(args, step):
+    """Run `step` (one bounded sample; returns (work units, seconds)) W times
+    untimed and K times timed; (units per second, mean seconds per step)."""
+    for _ in range(args.warmup):
+        step()
+    units = secs = 0.0
+    for _ in range(args.steps):
+        u, t = step()
+        units += u
+        secs += t
+    return units / secs, secs / args.steps
+
+
 def reference_arm(args, world):
-    """The reference's CPU route (restated in oracle/ and torch CPU), bounded sample."""
+    """The reference's CPU route for the workload (its torch host path,
+    restated in oracle/ and torch CPU) on the host cores with all threads,
+    rank 0 only: --warmup untimed and --steps timed steps, each a bounded
+    sample of the workload; value in this repo's metric and unit."""
     torch.set_num_threads(os.cpu_count() or 1)
-    if args.workload == "dfmp2":
+    threads = torch.get_num_threads()
+    wl = args.workload
+    per_step = max(0.3, min(2.0, 60.0 / max(args.steps + args.warmup, 1)))  # seconds per sample
+    # other workloads: one bounded sample (one step), timed on the wall clock
+    t0 = time.perf_counter()
+    if wl == "dfmp2":
         cb = cpu_dfmp2_sample(*DFMP2_DIMS, budget_s=8.0)
         nb, no, na = DFMP2_DIMS
-        return {"impl": "reference", "metric": f"DF-MP2 energy ms ({nb}/{no}/{na}, end to end)",
-                "value": cb["value"], "unit": "ms", "higher_is_better": False, "n_gpus": world,
-                "steps": 1, "warmup": 1, "config": {"workload": "dfmp2"}, "cpu_baseline": cb,
-                "e2e": {"value": cb["value"], "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    if args.workload in PAIR_DIMS:
-        dims = PAIR_DIMS[args.workload]
+        return _ref_line(args, world, f"DF-MP2 energy ms ({nb}/{no}/{na}, end to end)", "ms", False,
+                         cb["value"], (time.perf_counter() - t0) * 1e3, cb, steps=1, warmup=0)
+    if wl in PAIR_DIMS:
+        dims = PAIR_DIMS[wl]
         ms, th, sample = cpu_pair_sample(*dims, budget_s=8.0)
-        return {"impl": "reference", "metric": f"DF-MP2 pair-energy step ms ({dims[0]}/{dims[1]}/{dims[2]})",
-                "value": round(ms, 1), "unit": "ms", "higher_is_better": False, "n_gpus": world,
-                "steps": 1, "warmup": 1, "config": {"workload": args.workload},
-                "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port", "sample": sample},
-                "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    if args.workload in ("batched", "syrk", "gemm_fp64", "batched_bf16", "syrk_bf16", "gemm1024"):
-        cb = cpu_single_sample(args.workload, budget_s=8.0)
-        return {"impl": "reference", "metric": f"{args.workload} TFLOP/s", "value": cb["value"], "unit": "TFLOP/s",
-                "higher_is_better": True, "n_gpus": world, "steps": 1, "warmup": 1,
-                "config": {"workload": args.workload}, "cpu_baseline": cb,
-                "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    dt = torch.float32 if args.workload in ("gemm_fp32", "gemm8192_fp32") else torch.bfloat16
-    n = 32768 if args.workload in ("spmd", "gemm_fp32") else 8192
-    vals = []
-    for _ in range(max(1, min(args.steps, 2))):
-        v, th, sample = cpu_gemm_sample(n, dt, budget_s=8.0)
-        vals.append(v)
-    v = statistics.median(vals)
-    return {"impl": "reference", "metric": f"GEMM TFLOP/s (M=N=K={n}, {str(dt).split('.')[-1]})",
-            "value": round(v, 4), "unit": "TFLOP/s", "higher_is_better": True, "n_gpus": world,
-            "steps": len(vals), "warmup": 1, "config": {"workload": args.workload, "M": n, "N": n, "K": n},
-            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
-                             "sample": sample + " (torch CPU matmul: the reference's host route)"},
-            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        cb = {"unit": "ms", "cores": th, "kind": "port", "sample": sample}
+        return _ref_line(args, world, pair_metric(*dims), "ms", False, round(ms, 1),
+                         (time.perf_counter() - t0) * 1e3, cb, steps=1, warmup=0)
+    if wl in ("batched", "syrk", "gemm_fp64", "batched_bf16", "syrk_bf16", "gemm1024"):
+        cb = cpu_single_sample(wl, budget_s=8.0)
+        return _ref_line(args, world, f"{wl} TFLOP/s", "TFLOP/s", True, cb["value"],
+                         (time.perf_counter() - t0) * 1e3, cb, steps=1, warmup=0)
+    dt = torch.float32 if wl in ("gemm_fp32", "gemm8192_fp32") else torch.bfloat16
+    n = 32768 if wl in ("spmd", "gemm_fp32") else 8192
+    g = torch.Generator().manual_seed(5)
+    B = (2 * torch.rand(n, n, generator=g) - 1).to(dt)
+    A = (2 * torch.rand(64, n, generator=g) - 1).to(dt)
+    torch.matmul(A, B)  # thread-pool warm-up
+    t0 = time.perf_counter()
+    torch.matmul(A, B)
+    per_row = max((time.perf_counter() - t0) / 64, 1e-6)
+    rows = int(max(64, min(n, per_step / per_row)))
+    A = (2 * torch.rand(rows, n, generator=g) - 1).to(dt)
+
+    def step():
+        t = time.perf_counter()
+        torch.matmul(A, B)
+        return 2.0 * rows * n * n, time.perf_counter() - t
+
+    rate, sec = _ref_steps(args, step)
+    v = round(rate / 1e12, 4)
+    cb = {"unit": "TFLOP/s", "cores": threads, "kind": "port",
+          "sample": f"{rows} x {n} rows of the {n}^3 product per step, {dt} (torch CPU matmul: the reference's host route)"}
+    extra = None
+    if wl == "spmd" and not args.no_pair:
+        ms, th, sample = cpu_pair_sample(96, 2208, 6912, budget_s=8.0)
+        extra = {"pair_energy": {"metric": pair_metric(96, 2208, 6912), "value": round(ms, 1), "unit": "ms",
+                                 "higher_is_better": False, "steps": 1, "warmup": 0,
+                                 "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port",
+                                                  "sample": sample}}}
+    return _ref_line(args, world, gemm_metric(n, dt), "TFLOP/s", True, v, sec * 1e3, cb, extra)
 
 
 if __name__ == "__main__":

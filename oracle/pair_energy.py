@@ -113,3 +113,59 @@ def make_inputs(nocc: int, nvir: int, naux: int, seed: int, sigma: float = 0.05)
     eo = torch.sort(-20.0 + 19.7 * torch.rand(nocc, generator=g)).values
     ev = torch.sort(0.1 + 4.9 * torch.rand(nvir, generator=g)).values
     return B, eo, ev
+
+
+# ── the same arithmetic in torch, on any device (fp64 references at sizes
+#    the numpy loops cannot reach in seconds; still test infrastructure) ──
+
+
+def aten_rows_torch(B, eps_occ, eps_vir, rows, dtype=None, mem_budget_bytes: int = 1_500_000_000):
+    """trnblas/nki/multicore.py:263-289 (`aten_rows`, the chunked aten energy
+    of `_torch_chunked_pair_energy`, dispatch.py:2706-2728, restricted to
+    occupied rows [i0, i1)): sum over i in rows and every j of e_ij, in
+    `dtype` (default B's) on B's device. Same op order: T chunk = B_flat[rows]
+    @ B_flat^T, permuted to (i, j, a, b), sum T (2T - T^T) / (eps_o_pair -
+    eps_v_pair)."""
+    import torch
+
+    dtype = dtype or B.dtype
+    B = B.to(dtype)
+    eo, ev = eps_occ.to(B.device, dtype), eps_vir.to(B.device, dtype)
+    nocc, nvir, naux = B.shape
+    i0, i1 = rows
+    i_block = max(1, min(nocc, int(mem_budget_bytes // (4 * nvir * nocc * nvir))))
+    B_flat = B.reshape(nocc * nvir, naux)
+    eps_o_pair = eo.view(nocc, 1, 1, 1) + eo.view(1, nocc, 1, 1)
+    eps_v_pair = ev.view(1, 1, nvir, 1) + ev.view(1, 1, 1, nvir)
+    e = torch.zeros((), dtype=dtype, device=B.device)
+    for a in range(i0, i1, i_block):
+        b = min(a + i_block, i1)
+        T = (B_flat[a * nvir : b * nvir] @ B_flat.T).reshape(b - a, nvir, nocc, nvir)
+        T = T.permute(0, 2, 1, 3)
+        e = e + (T * (2.0 * T - T.transpose(-2, -1)) / (eps_o_pair[a:b] - eps_v_pair)).sum()
+    return float(e)
+
+
+def pair_range_energy_torch(B, eps_occ, eps_vir, pair_begin: int, pair_end: int, dtype=None) -> float:
+    """`pair_range_energy` (sum of w_p e_ij over a range of the i <= j pair
+    list) with the per-pair arithmetic of `_torch_chunked_pair_energy`
+    (T = B_i B_j^T, T (2T - T^T) / (e_i + e_j - e_a - e_b)), in `dtype`
+    (default B's) on B's device; one GEMM per pair row j."""
+    import torch
+
+    dtype = dtype or B.dtype
+    eo, ev = eps_occ.to(B.device, dtype), eps_vir.to(B.device, dtype)
+    tot = 0.0
+    p = pair_begin
+    while p < pair_end:
+        i, j = pair_index(p)
+        i_end = min(j + 1, i + (pair_end - p))
+        Bi = B[i:i_end].to(dtype)
+        Bj = B[j].to(dtype)
+        T = (Bi.reshape(-1, Bi.shape[-1]) @ Bj.T).reshape(i_end - i, Bj.shape[0], Bj.shape[0])
+        den = (eo[i:i_end].view(-1, 1, 1) + eo[j]) - ev.view(1, -1, 1) - ev.view(1, 1, -1)
+        e = (T * (2.0 * T - T.transpose(-2, -1)) / den).sum(dim=(1, 2))
+        w = torch.where(torch.arange(i, i_end, device=B.device) == j, 1.0, 2.0).to(dtype)
+        tot += float((w * e).sum())
+        p += i_end - i
+    return tot

@@ -1,6 +1,7 @@
 """CPU checks of the measurement plumbing in bench.py: the clock sampler's
 timed-region summary, the per-launch traffic figures the roofline objects
-read from profiles/, and the profile summaries' commands (ncu always with
+carry (equal to the profiles/ summaries'), the shared metric names of both
+arms, and the profile summaries' commands (ncu always with
 --clock-control none, committed files only)."""
 
 from __future__ import annotations
@@ -39,11 +40,40 @@ def test_clock_summary_keeps_the_timed_region(bench):
     assert cs.summary()["samples"] == 4
 
 
-def test_roofline_traffic_profiles_exist(bench):
-    names = set(bench.TRAFFIC_PROFILE.values()) | {"pair_energy_pair3"}
-    for name in sorted(names):
-        t = bench.read_traffic(name)
-        assert isinstance(t, int) and t > 0, name
+def _profile_traffic(name):
+    for ln in (ROOT / "profiles" / f"{name}.md").read_text().splitlines():
+        if ln.strip().startswith("traffic_bytes_per_launch:"):
+            return int(float(ln.split(":", 1)[1]))
+    return None
+
+
+def test_roofline_traffic_matches_profiles(bench):
+    """bench.py carries each per-launch traffic figure (it reads no profile at
+    run time); every figure equals the one in the summary its comment names."""
+    src = (ROOT / "bench.py").read_text()
+    table = src.split("TRAFFIC = {", 1)[1].split("}", 1)[0]
+    for line in table.strip().splitlines():
+        key, rest = line.split(":", 1)
+        key = key.strip().strip('"')
+        assert "# profiles/" in rest, key
+        prof = rest.split("# profiles/", 1)[1].split(".md", 1)[0]
+        assert bench.TRAFFIC[key] == _profile_traffic(prof), (key, prof)
+
+
+def test_both_arms_name_the_same_metric(bench):
+    """The driver divides the two arms' values only when metric, unit and
+    direction agree: both arms take the metric string from the same helper."""
+    import inspect
+
+    import torch
+
+    assert bench.gemm_metric(32768, torch.bfloat16) == "GEMM TFLOP/s (M=N=K=32768, bfloat16)"
+    ours = inspect.getsource(bench.run_gemm_spmd)
+    ref = inspect.getsource(bench.reference_arm)
+    assert '"metric": gemm_metric(n, dtype)' in ours and "gemm_metric(n, dt)" in ref
+    assert "pair_metric(96, 2208, 6912)" in inspect.getsource(bench.run_ours)
+    assert "pair_metric(96, 2208, 6912)" in ref
+    assert "read_traffic" not in (ROOT / "bench.py").read_text()
 
 
 @pytest.mark.parametrize("path", sorted((ROOT / "profiles").glob("*.md")), ids=lambda p: p.name)

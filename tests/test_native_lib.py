@@ -61,6 +61,54 @@ def test_argument_errors_without_gpu():
     assert L.trnblas_gemm(N.F32, 1, 0, 4, 4, 1.0, None, 4, 0, 0, None, 4, 0, 0, 0.0, None, 0, 0, None, 4, 0, None, 0, None) == 0
 
 
+FAKE = 1 << 20  # a non-NULL address that the argument checks reject before any use
+
+
+@pytest.mark.parametrize("dtype", [N.F32, N.BF16, N.F16])
+@pytest.mark.parametrize("lda,ldb,ta,tb", [(3, 8, 0, 0), (8, 3, 0, 0), (-8, 8, 0, 0), (8, 4, 1, 0), (8, 7, 0, 1)])
+def test_gemm_leading_dimensions_checked_for_every_dtype(dtype, lda, ldb, ta, tb):
+    """lda / ldb below the stored row length (A: K, or M when transposed; B: N,
+    or K when transposed) or negative are refused before any device work, for
+    the fp32 split path as well as the 16-bit TMA path. M = 8, N = 8, K = 4,
+    except the transposed cases, where the short leading dimension is set
+    against M = 8 (A) or K = 8 (B)."""
+    L = N.lib()
+    M, Nn, K = (8, 8, 4) if not ta and not tb else ((8, 8, 8))
+    rc = L.trnblas_gemm(dtype, 1, M, Nn, K, 1.0, FAKE, lda, 0, ta, FAKE, ldb, 0, tb, 0.0, None, 0, 0,
+                        FAKE, Nn, 0, FAKE, 1 << 20, None)
+    assert rc == N.ERR_ARG and "lda/ldb" in N.last_error()
+
+
+def test_syrk_lda_checked_for_fp32():
+    L = N.lib()
+    rc = L.trnblas_syrk(N.F32, 8, 16, 1.0, FAKE, 8, 0, 0.0, None, 0, 0, FAKE, 8, FAKE, 1 << 20, None)
+    assert rc == N.ERR_ARG and "lda" in N.last_error()
+
+
+def test_gemm_k_limit():
+    L = N.lib()
+    rc = L.trnblas_gemm(N.F32, 1, 8, 8, (1 << 31) - 2, 1.0, FAKE, 1 << 31, 0, 0, FAKE, 8, 0, 0, 0.0, None, 0, 0,
+                        FAKE, 8, 0, FAKE, 1 << 20, None)
+    assert rc == N.ERR_ARG and "limit" in N.last_error()
+
+
+def test_noalloc_argument_checks_without_gpu():
+    """The allocation-free fp32 GEMM checks sizes before it touches the device:
+    leading dimensions as trnblas_gemm, dimensions at the limits (whose scratch
+    size would overflow a 64-bit product) and a problem too large for the
+    built-in scratch are refused."""
+    L = N.lib()
+    fn = L.trnblas_gemm_f32_noalloc
+    # lda below K (fp32 path checks it too)
+    assert fn(64, 64, 64, 1.0, FAKE, 32, 0, FAKE, 64, 0, 0.0, None, 0, FAKE, 64, None) == N.ERR_ARG
+    assert "lda/ldb" in N.last_error()
+    big = (1 << 31) - 1
+    assert fn(big, big, big - 3, 1.0, FAKE, big, 0, FAKE, big, 0, 0.0, None, 0, FAKE, big, None) == N.ERR_WORKSPACE
+    assert "scratch" in N.last_error()
+    assert fn(1 << 31, 8, 8, 1.0, FAKE, 8, 0, FAKE, 8, 0, 0.0, None, 0, FAKE, 8, None) == N.ERR_ARG
+    assert fn(4096, 4096, 4096, 1.0, FAKE, 4096, 0, FAKE, 4096, 0, 0.0, None, 0, FAKE, 4096, None) == N.ERR_WORKSPACE
+
+
 def test_dtype_codes():
     import torch
 

@@ -64,6 +64,11 @@ def test_host_inputs_and_errors():
     B, eo, ev = (torch.from_numpy(ZE[f"small_{k}"]) for k in ("B", "eo", "ev"))
     e = energy.batched_pair_energy(B, eo, ev)
     assert e.device.type == "cpu" and e.dtype == torch.float64 and e.dim() == 0
+    # the reference's entry point returns promote_types(B, eps_vir): float32 here
+    e32 = energy.nki_batched_pair_energy(B, eo, ev)
+    assert e32.device.type == "cpu" and e32.dtype == torch.float32 and e32.dim() == 0
+    assert float(e32) == float(e.float())
+    assert energy.nki_batched_pair_energy(B.double(), eo, ev.double()).dtype == torch.float64
     with pytest.raises(ValueError):
         energy.pair_range_energy(B, eo, ev, 5, 3)
     with pytest.raises(ValueError):

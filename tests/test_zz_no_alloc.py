@@ -6,7 +6,14 @@ cudaMalloc's device synchronisation is not allowed): its split scratch is an
 array built into the library. The test compares it with the ordinary
 trnblas_gemm (caller-provided workspace) on two calls in a row, so the second
 call runs on scratch that still holds the first call's contents, and checks
-that an over-size problem is refused. Collected last on purpose.
+that an over-size problem is refused. With a second GPU it repeats the
+comparison with that GPU current, where the library looks up the array's
+address on that device for the first time.
+
+The file name sorts last so that pytest collects it after every other test:
+a run that stops at the first failure (-x) has then already run the rest of
+the suite, and a failure here cannot hide another. It also runs alone in a
+fresh process.
 """
 
 from __future__ import annotations
@@ -44,23 +51,34 @@ def _with_workspace(A, B, C, alpha, beta, transA, transB, M, N_, K):
     return rc, D
 
 
-def test_noalloc_matches_trnblas_gemm_on_two_calls():
-    g = torch.Generator(device="cuda").manual_seed(11)
+def _two_calls(dev: torch.device):
+    g = torch.Generator(device=dev).manual_seed(11)
     cases = [(300, 200, 517, False, False), (1024, 768, 1536, True, True)]  # 2nd call reuses scratch
     for M, N_, K, ta, tb in cases:
-        A = torch.randn(*((K, M) if ta else (M, K)), device="cuda", generator=g)
-        B = torch.randn(*((N_, K) if tb else (K, N_)), device="cuda", generator=g)
-        C = torch.randn(M, N_, device="cuda", generator=g)
+        A = torch.randn(*((K, M) if ta else (M, K)), device=dev, generator=g)
+        B = torch.randn(*((N_, K) if tb else (K, N_)), device=dev, generator=g)
+        C = torch.randn(M, N_, device=dev, generator=g)
         rc1, D1 = _noalloc(A, B, C, 0.75, -0.5, ta, tb, M, N_, K)
         rc2, D2 = _with_workspace(A, B, C, 0.75, -0.5, ta, tb, M, N_, K)
         assert rc1 == 0, N.last_error()
         assert rc2 == 0, N.last_error()
-        torch.cuda.synchronize()
+        torch.cuda.synchronize(dev)
         assert _relf(D1, D2) <= TOL
         a = A.double().T if ta else A.double()
         b = B.double().T if tb else B.double()
         assert _relf(D1, 0.75 * a @ b - 0.5 * C.double()) <= TOL
-    assert N.device_status(0) == 0
+    assert N.device_status(dev.index) == 0
+
+
+def test_noalloc_matches_trnblas_gemm_on_two_calls():
+    _two_calls(torch.device("cuda", 0))
+
+
+def test_noalloc_on_second_device():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs a second GPU")
+    with torch.cuda.device(1):
+        _two_calls(torch.device("cuda", 1))
 
 
 def test_noalloc_rejects_oversize_problem():

@@ -48,22 +48,3 @@ def device_status(device=None) -> int:
     """Synchronise and read (then clear) the device's kernel status word."""
     return _native.device_status(device)
 
-
-__all__ = [
-    "batched_gemm",
-    "batched_pair_energy",
-    "device_status",
-    "diag_flag",
-    "energy",
-    "gemm",
-    "gemm_fp64",
-    "get_backend",
-    "nki_batched_pair_energy",
-    "pair_range_energy",
-    "parallel",
-    "set_backend",
-    "side_flag",
-    "syrk",
-    "trans_flag",
-    "uplo_flag",
-]

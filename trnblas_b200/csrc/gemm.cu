@@ -212,8 +212,10 @@ int check_dims(long long batch, long long M, long long N, long long K) {
     return TRNBLAS_ERR_ARG;
   }
   const long long lim = (1ll << 31) - 1;
-  if (M > lim || N > lim || K > lim || batch > 65535ll * 65535ll) {
-    set_error("size exceeds the 2^31-1 element limit per dimension");
+  // K is padded to a multiple of 4 for the fp32 split planes and the padded
+  // length is used as an int (kernel arguments, tensor-map row stride)
+  if (M > lim || N > lim || K > (lim & ~3ll) || batch > 65535ll * 65535ll) {
+    set_error("size exceeds the element limit per dimension (2^31-1; K: 2^31-4)");
     return TRNBLAS_ERR_ARG;
   }
   return TRNBLAS_OK;
@@ -306,6 +308,17 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
     set_error("trnblas_gemm: ldc/ldd smaller than N");
     return TRNBLAS_ERR_ARG;
   }
+  // Stored row lengths: A is M x K (K x M when transposed), B is K x N
+  // (N x K when transposed). Every dtype reads rows of that length at stride
+  // ld (the fp32 split kernels as well as the TMA maps), so a shorter or
+  // negative ld would read outside the operand.
+  {
+    const long long a_cols = transA ? M : K, b_cols = transB ? K : N;
+    if (K > 0 && (lda < a_cols || ldb < b_cols || lda < 1 || ldb < 1)) {
+      set_error("trnblas_gemm: lda/ldb smaller than the stored row length");
+      return TRNBLAS_ERR_ARG;
+    }
+  }
   int* status = status_word();
   if (!status) return TRNBLAS_ERR_CUDA;
   const int out_kind = dtype == TRNBLAS_F32 ? kOutF32 : dtype == TRNBLAS_BF16 ? kOutBF16 : kOutF16;
@@ -385,12 +398,8 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   p.a_mn = transA ? 1 : 0;   // A stored K x M: M contiguous
   p.b_mn = transB ? 0 : 1;   // B stored K x N: N contiguous
   p.in_fmt = dtype == TRNBLAS_BF16 ? kFmtBF16 : kFmtF16;
-  const long long a_rows = transA ? K : M, a_cols = transA ? M : K;
-  const long long b_rows = transB ? N : K, b_cols = transB ? K : N;
-  if (lda < a_cols || ldb < b_cols) {
-    set_error("trnblas_gemm: lda/ldb smaller than the stored row length");
-    return TRNBLAS_ERR_ARG;
-  }
+  const long long a_rows = transA ? K : M;
+  const long long b_rows = transB ? N : K;
   const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 8);
   const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 8);
   bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)
@@ -427,6 +436,12 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
   const bool use_c = C && beta != 0.0f && c_uplo != 0;
   if (!D || (k > 0 && !A) || ldd < n || (use_c && ldc < n)) {
     set_error("trnblas_syrk: NULL operand or leading dimension smaller than n");
+    return TRNBLAS_ERR_ARG;
+  }
+  // A is stored n x k (k x n when trans); every dtype reads rows of that
+  // length at stride lda
+  if (k > 0 && (lda < (trans ? n : k) || lda < 1)) {
+    set_error("trnblas_syrk: lda smaller than the stored row length");
     return TRNBLAS_ERR_ARG;
   }
   int* status = status_word();
@@ -480,11 +495,7 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
   const auto dt = map_dtype(dtype);
   p.a_mn = p.b_mn = trans ? 1 : 0;
   p.in_fmt = dtype == TRNBLAS_BF16 ? kFmtBF16 : kFmtF16;
-  const long long rows = trans ? k : n, cols = trans ? n : k;
-  if (lda < cols) {
-    set_error("trnblas_syrk: lda smaller than the stored row length");
-    return TRNBLAS_ERR_ARG;
-  }
+  const long long rows = trans ? k : n;
   const long long s2 = round_up(lda * rows, 8);
   // 128 x 256 tiles over the lower triangle's column-block pairs: half the
   // operand bytes per MMA of 128 x 128 tiles, and half the tiles

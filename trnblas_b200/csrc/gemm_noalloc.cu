@@ -70,6 +70,32 @@ int trnblas_gemm_f32_noalloc(int64_t M, int64_t N, int64_t K, float alpha, const
     tb::set_error("trnblas_gemm_f32_noalloc: negative size");
     return TRNBLAS_ERR_ARG;
   }
+  const long long lim = (1ll << 31) - 1;
+  if (M > lim || N > lim || K > (lim & ~3ll)) {
+    tb::set_error("trnblas_gemm_f32_noalloc: size exceeds the element limit per dimension "
+                  "(2^31-1; K: 2^31-4)");
+    return TRNBLAS_ERR_ARG;
+  }
+  // The split planes take 8 * (M + N) * round_up(K, 4) bytes (plus at most
+  // 1 KiB of alignment padding). Compared by division first, so that sizes
+  // near the dimension limits cannot overflow the product into a small value.
+  const long long kp = tb::round_up(K > 0 ? K : 1, 4);
+  if (K > 0 && M > 0 && N > 0 &&
+      M + N > static_cast<long long>(tb::kNoAllocScratchBytes / 8) / kp) {
+    tb::set_error("trnblas_gemm_f32_noalloc: the problem needs more than the built-in " +
+                  std::to_string(tb::kNoAllocScratchBytes) +
+                  " scratch bytes (8 * (M + N) * round_up(K, 4) must fit); use trnblas_gemm "
+                  "with a caller workspace");
+    return TRNBLAS_ERR_WORKSPACE;
+  }
+  // Leading dimensions as trnblas_gemm checks them, before the scratch
+  // address lookup (which needs the device) so a bad call fails as ERR_ARG.
+  if (M > 0 && N > 0 && K > 0 &&
+      (lda < (transA ? M : K) || ldb < (transB ? K : N) || ldd < N ||
+       (C && beta != 0.0f && ldc < N))) {
+    tb::set_error("trnblas_gemm_f32_noalloc: lda/ldb/ldc/ldd smaller than the stored row length");
+    return TRNBLAS_ERR_ARG;
+  }
   const size_t need = trnblas_gemm_workspace_size(TRNBLAS_F32, 1, M, N, K, 0, 0);
   if (need > tb::kNoAllocScratchBytes) {
     tb::set_error("trnblas_gemm_f32_noalloc: the problem needs " + std::to_string(need) +

@@ -93,5 +93,13 @@ def batched_pair_energy(B: torch.Tensor, eps_occ: torch.Tensor, eps_vir: torch.T
     return e.to(home) if home != e.device else e  # a 0-d result: nothing to stream
 
 
-# The reference's name for the same entry point.
-nki_batched_pair_energy = batched_pair_energy
+def nki_batched_pair_energy(B: torch.Tensor, eps_occ: torch.Tensor, eps_vir: torch.Tensor) -> torch.Tensor:
+    """The reference's entry point (trnblas/nki/dispatch.py:2537-2569): the
+    total pair energy as a 0-d tensor on B's device in the dtype the
+    reference returns, torch.promote_types(B.dtype, eps_vir.dtype)
+    (`_pair_result_dtype`, dispatch.py:1334-1340; float32 for float32
+    inputs). The kernel's fp64 sum is rounded to that dtype at the end;
+    `batched_pair_energy` returns it unrounded."""
+    e = batched_pair_energy(B, eps_occ, eps_vir)
+    dt = torch.promote_types(B.dtype, eps_vir.dtype)
+    return e.to(dt) if (dt.is_floating_point and e.dtype != dt) else e

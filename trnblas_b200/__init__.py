@@ -10,7 +10,7 @@ from __future__ import annotations
 
 from . import _native
 from ._flags import diag_flag, side_flag, trans_flag, uplo_flag
-from . import energy, parallel
+from . import energy, ops, parallel
 from .energy import batched_pair_energy, nki_batched_pair_energy, pair_range_energy
 from .level3 import batched_gemm, gemm, gemm_fp64, metric_inv_half, symm, syrk, trmm, trsm
 
@@ -19,7 +19,7 @@ __version__ = "0.1.0"
 __all__ = [
     "gemm", "batched_gemm", "syrk", "gemm_fp64", "trsm", "metric_inv_half", "symm", "trmm",
     "batched_pair_energy", "nki_batched_pair_energy", "pair_range_energy",
-    "energy", "parallel",
+    "energy", "ops", "parallel",
     "trans_flag", "uplo_flag", "side_flag", "diag_flag",
     "set_backend", "get_backend", "device_status",
 ]

@@ -3,7 +3,10 @@
 #include <algorithm>
 #include <string>
 
+#include <cstdlib>
+
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_pair.cuh"
 #include "runtime.hpp"
 
 namespace tb {
@@ -198,7 +201,59 @@ int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   return TRNBLAS_OK;
 }
 
+// The CTA-pair kernel: clusters of two CTAs, as many pairs as can be
+// resident at once (the persistent tile walk needs every pair running).
+template <int STAGES>
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, cudaStream_t stream) {
+  using Cfg = PairGemmCfg<STAGES>;
+  constexpr int smem = Cfg::SMEM;
+  auto kern = gemm_pair_kernel<STAGES>;
+  static int max_pairs[64] = {};
+  const int dev = current_device();
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dev < 0 || dev >= 64 || !max_pairs[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair gemm smem)");
+    cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters(pair gemm)");
+    if (clusters < 1) {
+      set_error("pair gemm: no CTA pair fits on this device");
+      return TRNBLAS_ERR_CUDA;
+    }
+    if (dev >= 0 && dev < 64) max_pairs[dev] = clusters;
+    else return TRNBLAS_ERR_CUDA;
+  }
+  const int pairs = static_cast<int>(std::min<long long>(p.num_tiles, max_pairs[dev]));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p);
+  if (e != cudaSuccess) return cuda_fail(e, "pair gemm kernel launch");
+  return TRNBLAS_OK;
+}
+
 bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBLAS_F16; }
+
+// CTA-pair tiles (256 x 256) for 16-bit GEMMs with at least two 128-row and
+// two 128-column blocks; TRNBLAS_B200_GEMM_PAIR=0 keeps the one-CTA kernel.
+bool use_pair_gemm(long long M, long long N) {
+  static const int mode = [] {
+    const char* s = std::getenv("TRNBLAS_B200_GEMM_PAIR");
+    return (s && *s) ? std::atoi(s) : -1;
+  }();
+  if (mode == 0) return false;
+  return M > 128 && N > 128;
+}
 
 // Bytes of one fp32 split plane (R x Kp) for `nb` batch entries, 256-aligned.
 size_t plane_bytes(long long nb, long long R, long long K) {
@@ -393,7 +448,6 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   }
 
   // bf16 / fp16: operands straight from their own layout.
-  const int bn = pick_bn(batch, M, N);
   const auto dt = map_dtype(dtype);
   p.a_mn = transA ? 1 : 0;   // A stored K x M: M contiguous
   p.b_mn = transB ? 0 : 1;   // B stored K x N: N contiguous
@@ -402,6 +456,21 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   const long long b_rows = transB ? N : K;
   const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 8);
   const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 8);
+  if (use_pair_gemm(M, N)) {
+    // 256 x 256 tiles on CTA pairs; each CTA loads 128 rows of A and 128
+    // columns of B
+    bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)
+                     : encode_map_3d(&ma0, dt, 2, A, K, M, nba, lda, sa2, 64, 128);
+    ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 2, B, N, K, nbb, ldb, sb2, 64, 64)
+                       : encode_map_3d(&mb0, dt, 2, B, K, N, nbb, ldb, sb2, 64, 128));
+    if (!ok) return TRNBLAS_ERR_ALIGN;
+    p.group_m = 8;
+    p.tiles_m = static_cast<int>(ceil_div(M, 256));
+    p.tiles_n = static_cast<int>(ceil_div(N, 256));
+    p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+    return launch_gemm_pair<6>(ma0, mb0, p, stream);
+  }
+  const int bn = pick_bn(batch, M, N);
   bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)
                    : encode_map_3d(&ma0, dt, 2, A, K, M, nba, lda, sa2, 64, 128);
   ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 2, B, N, K, nbb, ldb, sb2, 64, 64)

@@ -181,6 +181,30 @@ CUtensorMapDataType map_dtype(int dtype) {
   }
 }
 
+// Tile-walk band width (row tiles per band of the grouped order);
+// TRNBLAS_B200_GEMM_GROUP_M overrides it (tuning).
+int group_m_override() {
+  static const int g = [] {
+    const char* s = std::getenv("TRNBLAS_B200_GEMM_GROUP_M");
+    const int v = (s && *s) ? std::atoi(s) : 0;
+    return v > 0 ? v : 0;
+  }();
+  return g;
+}
+
+// Soft tile-wave synchronisation (soft_wave_wait) for long K loops with at
+// least two waves of tiles. Measured on a 32768^3 bf16 product under the 1 kW
+// power cap (one-CTA kernel, band of 16 row tiles): DRAM reads per launch
+// 144 -> 69 GB; the same box went 1145 -> 1209 TFLOP/s.
+// TRNBLAS_B200_GEMM_WAVESYNC = 0 / 1 overrides the default (on).
+bool use_wave_sync(long long K, long long tiles, long long grid) {
+  static const int mode = [] {
+    const char* s = std::getenv("TRNBLAS_B200_GEMM_WAVESYNC");
+    return (s && *s) ? std::atoi(s) : 1;
+  }();
+  return mode != 0 && K >= 4096 && tiles >= 2 * grid;
+}
+
 template <int KIND, int BN, int STAGES>
 int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
                 const CUtensorMap& b1, GemmParams& p, cudaStream_t stream) {
@@ -195,6 +219,7 @@ int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int grid = static_cast<int>(std::min<long long>(p.num_tiles, num_sms()));
+  if (p.mode == kModeGemm && use_wave_sync(p.K, p.num_tiles, grid)) p.wave_ctr = wave_counter(stream);
   kern<<<grid, 192, smem, stream>>>(a0, a1, b0, b1, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
@@ -237,6 +262,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, 
   }
   const int pairs = static_cast<int>(std::min<long long>(p.num_tiles, max_pairs[dev]));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  if (use_wave_sync(p.K, p.num_tiles, pairs)) p.wave_ctr = wave_counter(stream);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p);
   if (e != cudaSuccess) return cuda_fail(e, "pair gemm kernel launch");
   return TRNBLAS_OK;
@@ -245,14 +271,18 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, 
 bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBLAS_F16; }
 
 // CTA-pair tiles (256 x 256) for 16-bit GEMMs with at least two 128-row and
-// two 128-column blocks; TRNBLAS_B200_GEMM_PAIR=0 keeps the one-CTA kernel.
+// two 128-column blocks, when TRNBLAS_B200_GEMM_PAIR=1. Not the default: the
+// pair kernel keeps the tensor pipe busier per clock (8192^3: 92 % of cycles
+// against 76 %, 1439 against 1323 TFLOP/s at full clock), but it spends more
+// energy per flop, so under the 1 kW power cap of a sustained run its clock
+// falls further and it finishes later (32768^3: 0.89-0.98 TFLOP per joule
+// against 1.19-1.34 for the one-CTA kernel, measured on the same box).
 bool use_pair_gemm(long long M, long long N) {
   static const int mode = [] {
     const char* s = std::getenv("TRNBLAS_B200_GEMM_PAIR");
-    return (s && *s) ? std::atoi(s) : -1;
+    return (s && *s) ? std::atoi(s) : 0;
   }();
-  if (mode == 0) return false;
-  return M > 128 && N > 128;
+  return mode == 1 && M > 128 && N > 128;
 }
 
 // Bytes of one fp32 split plane (R x Kp) for `nb` batch entries, 256-aligned.
@@ -403,7 +433,9 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   p.D = D;
   p.ldd = ldd;
   p.strideD = strideD;
-  p.group_m = 16;
+  // bands of 12 row tiles: with the wave synchronisation, the lowest energy
+  // per flop measured at 32768^3 under the power cap (widths 4 .. 16 swept)
+  p.group_m = group_m_override() ? group_m_override() : 12;
   p.status = status;
   p.timeout_ns = wait_timeout_ns();
   const bool a_b = strideA != 0 && batch > 1;
@@ -464,7 +496,7 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
     ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 2, B, N, K, nbb, ldb, sb2, 64, 64)
                        : encode_map_3d(&mb0, dt, 2, B, K, N, nbb, ldb, sb2, 64, 128));
     if (!ok) return TRNBLAS_ERR_ALIGN;
-    p.group_m = 8;
+    p.group_m = group_m_override() ? group_m_override() : 8;
     p.tiles_m = static_cast<int>(ceil_div(M, 256));
     p.tiles_n = static_cast<int>(ceil_div(N, 256));
     p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);

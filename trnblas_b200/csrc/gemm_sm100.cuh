@@ -58,7 +58,24 @@ struct GemmParams {
   int group_m;
   int* status;
   unsigned long long timeout_ns;
+  int* wave_ctr;  // tile-wave synchronisation counter (nullptr: none)
 };
+
+// Soft wave barrier of the persistent tile walk: the producer waits until
+// every CTA has issued the loads of its previous tile (`target` arrivals on
+// the launch's counter), so the CTAs of a wave start their tiles together and
+// read the operand slabs they share while those are still in L2 (left alone,
+// CTAs drift apart over a long K loop and each re-reads from DRAM what the
+// others loaded). Only a performance hint: after `limit_ns` the producer goes
+// on regardless, so a CTA that is not resident cannot hold the others up.
+__device__ __forceinline__ void soft_wave_wait(const int* ctr, int target,
+                                               unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (*reinterpret_cast<const volatile int*>(ctr) < target) {
+    if (globaltimer_ns() - t0 > limit_ns) break;
+    __nanosleep(128);
+  }
+}
 
 // Shared memory after the pipeline stages: 256 bytes of barriers, then one
 // 4 KB transpose stage per epilogue warp (SYRK mirror stores).
@@ -442,7 +459,10 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t phase = 0;
     // armed-but-unobserved stages (for the drain on abort)
     bool aborted = false;
-    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x) {
+    int wave = 0;
+    for (int t = blockIdx.x; t < p.num_tiles && !aborted; t += gridDim.x, ++wave) {
+      if (p.wave_ctr && wave > 0)
+        soft_wave_wait(p.wave_ctr, wave * static_cast<int>(gridDim.x), 100000ull);
       int bz, mb, nb;
       decode_tile(p, t, bz, mb, nb);
       const int m0 = mb * BM;
@@ -484,6 +504,7 @@ __global__ void __launch_bounds__(192, 1)
           phase ^= 1u;
         }
       }
+      if (p.wave_ctr) atomicAdd(p.wave_ctr, 1);
     }
     if (aborted || ab.raised()) {
       // Let copies already issued land before the CTA exits: wait (bounded)

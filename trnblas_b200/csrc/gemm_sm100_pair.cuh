@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(192, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool aborted = false;
-    for (int t = pair; t < p.num_tiles && !aborted; t += npairs) {
+    int wave = 0;
+    for (int t = pair; t < p.num_tiles && !aborted; t += npairs, ++wave) {
+      if (p.wave_ctr && wave > 0)
+        soft_wave_wait(p.wave_ctr, wave * static_cast<int>(gridDim.x), 100000ull);
       int bz, mb, nb;
       decode_tile(p, t, bz, mb, nb);
       const int m0 = mb * Cfg::BM + Cfg::HM * static_cast<int>(rank);
@@ -196,6 +199,7 @@ __global__ void __launch_bounds__(192, 1)
           phase ^= 1u;
         }
       }
+      if (p.wave_ctr) atomicAdd(p.wave_ctr, 1);
     }
     if (aborted || ab.raised()) {
       // Copies already issued complete on the leader's barriers, which this

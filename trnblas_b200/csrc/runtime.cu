@@ -4,6 +4,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -18,6 +19,12 @@ thread_local std::string g_last_error;
 // One status word per device. Device code writes it with atomicCAS on the
 // first failure; trnblas_device_status reads and clears it.
 __device__ int g_status_word;
+
+// Wave counters of the GEMM's tile-walk synchronisation, one per launch slot
+// (slots rotate, so launches in flight on different streams count apart).
+constexpr int kWaveSlots = 64;
+__device__ int g_wave_ctr[kWaveSlots];
+std::atomic<unsigned> g_wave_next{0};
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
@@ -70,6 +77,23 @@ int* status_word() {
     g_status_ptr[d] = static_cast<int*>(p);
   }
   return g_status_ptr[d];
+}
+
+int* wave_counter(cudaStream_t stream) {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return nullptr;
+  static int* base[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!base[d]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_wave_ctr) != cudaSuccess) return nullptr;
+      base[d] = static_cast<int*>(p);
+    }
+  }
+  int* c = base[d] + (g_wave_next.fetch_add(1) % kWaveSlots);
+  if (cudaMemsetAsync(c, 0, sizeof(int), stream) != cudaSuccess) return nullptr;
+  return c;
 }
 
 int num_sms() {

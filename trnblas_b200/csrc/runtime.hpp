@@ -23,6 +23,9 @@ int cuda_fail(cudaError_t e, const char* what);
 // Per-device kernel status word (device memory, zero when healthy).
 int* status_word();            // current device; nullptr on failure (error set)
 int num_sms();                 // current device
+// A zeroed (stream-ordered) counter for one launch's tile-wave
+// synchronisation on the current device; nullptr if unavailable.
+int* wave_counter(cudaStream_t stream);
 int current_device();
 
 // Encode a 3-D tiled tensor map with the 128-byte swizzle. dims/strides are in

@@ -74,3 +74,27 @@ def test_host_inputs_and_errors():
     with pytest.raises(ValueError):
         energy.batched_pair_energy(B[0], eo, ev)
     assert float(energy.pair_range_energy(B, eo, ev, 4, 4)) == 0.0
+
+
+@pytest.mark.parametrize("naux", [33280, 33281])
+def test_naux_limit_of_each_form(naux):
+    """naux up to 33280 runs the base-254 form (10 int8 products, exact int32
+    while 4 * 127^2 * naux < 2^31); above it the 7-bit form (15 products).
+    Both sides of the limit against the fp64 oracle."""
+    B, eo, ev = PE.make_inputs(2, 40, naux, 12)
+    Bd, eod, evd = _dev(B, eo, ev)
+    ref = PE.chunked_energy(B.numpy(), eo.numpy(), ev.numpy())
+    got = float(energy.batched_pair_energy(Bd, eod, evd))
+    assert abs(got - ref) <= TOL * abs(ref)
+
+
+def test_single_diagonal_pairs():
+    """Pairs i == j alone, where the base-254 truncation would bias the
+    diagonal elements T_aa (taken from exact fp64 row sums of squares)."""
+    B, eo, ev = PE.make_inputs(7, 300, 200, 9)
+    Bd, eod, evd = _dev(B, eo, ev)
+    for i in range(3):
+        p = i * (i + 1) // 2 + i
+        ref = PE.pair_range_energy(B.numpy(), eo.numpy(), ev.numpy(), p, p + 1)
+        got = float(energy.pair_range_energy(Bd, eod, evd, p, p + 1))
+        assert abs(got - ref) <= TOL * abs(ref), i

@@ -1,5 +1,10 @@
 // Fused DF-MP2 pair energy on the int8 tensor cores.
 //
+// Two digit forms share the pair walk, the work units and the host entry
+// point below: the base-254 form of pair_energy254.cuh (10 int8 products,
+// fp64 epilogue) for naux <= 33280, and the 7-bit form described here (15
+// products) for larger naux, up to 104857.
+//
 // E = sum over occupied pairs i <= j (weight 1 if i == j, else 2) of
 //     sum_{a,b} T_ab (2 T_ab - T_ba) / (e_i + e_j - e_a - e_b),  T = B_i B_j^T,
 // following the reference's symmetric pair walk (trnblas/nki/dispatch.py:
@@ -55,6 +60,7 @@ struct PairParams {
   int units_per_pair;
   int nR, nC;              // 128-blocks and 64-blocks of nvir
   const int* exps;         // nocc * nvir
+  const double* rowsq;     // nocc * nvir fp64 row sums of squares (base-254 form)
   const float* eps_occ;
   const float* eps_vir;
   double* partials;        // gridDim.x
@@ -401,6 +407,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
+}  // namespace tb
+
+#include "pair_energy254.cuh"
+
+namespace tb {
+
 // Sum the per-CTA partials in index order (deterministic).
 __global__ void pair_energy_finish(const double* partials, int n, double* energy) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
@@ -416,24 +428,33 @@ constexpr int kPairSlices = 5;
 constexpr int kPairStages = 6;
 constexpr int kMaxGrid = 1024;
 
+// naux up to Pe254::MAX_NAUX runs the base-254 form (10 int8 products per
+// 64-column block); larger naux the 7-bit form (15 products, exact int32 up
+// to 104857).
+bool use_pe254(long long naux) { return naux <= Pe254::MAX_NAUX; }
+
 struct PairLayout {
   long long naux_p, R, nv_pad, rows_pad;
-  size_t off_digb, off_exps, off_max, off_range, off_part, off_order, total;
+  int slices;
+  size_t off_digb, off_exps, off_max, off_range, off_rowsq, off_part, off_order, total;
 };
 
 PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long npairs) {
   PairLayout L{};
-  L.naux_p = round_up(std::max<long long>(naux, 1), 32);
+  const bool b254 = use_pe254(naux);
+  L.slices = b254 ? Pe254::KS : kPairSlices;
+  L.naux_p = round_up(std::max<long long>(naux, 1), b254 ? Pe254::SW : 32);
   L.R = nocc * nvir;
   L.nv_pad = round_up(std::max<long long>(nvir, 1), 128);
   L.rows_pad = nocc * L.nv_pad;
   // the digits twice: in 128-row blocks (A operand) and in 64-row blocks (B)
-  const size_t dig = static_cast<size_t>(round_up(kPairSlices * L.rows_pad * L.naux_p, 256));
+  const size_t dig = static_cast<size_t>(round_up(L.slices * L.rows_pad * L.naux_p, 256));
   L.off_digb = dig;
   L.off_exps = 2 * dig;
   L.off_max = L.off_exps + round_up(4 * L.R, 256);
   L.off_range = L.off_max + round_up(8 * L.R, 256);
-  L.off_part = L.off_range + 256;
+  L.off_rowsq = L.off_range + 256;
+  L.off_part = L.off_rowsq + round_up(8 * L.R, 256);
   L.off_order = L.off_part + round_up(8 * kMaxGrid, 256);
   L.total = L.off_order + round_up(8 * std::max<long long>(npairs, 1), 256);
   return L;
@@ -445,7 +466,7 @@ int pair_block(const PairLayout& L, long long nocc) {
   int l2 = 0;
   if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, current_device()) != cudaSuccess || l2 <= 0)
     l2 = 96 << 20;
-  const double per_orb = 2.0 * kPairSlices * static_cast<double>(L.nv_pad) * L.naux_p;
+  const double per_orb = 2.0 * L.slices * static_cast<double>(L.nv_pad) * L.naux_p;
   const long long g = static_cast<long long>(0.5 * l2 / (2.0 * per_orb));
   return static_cast<int>(std::max<long long>(1, std::min<long long>(g, std::max<long long>(nocc, 1))));
 }
@@ -528,9 +549,32 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
                   reinterpret_cast<int*>(ws + L.off_range)};
   double* partials = reinterpret_cast<double*>(ws + L.off_part);
   int2* order = reinterpret_cast<int2*>(ws + L.off_order);
-  cudaError_t e = launch_split_tiled(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux),
-                                     nvir, L.nv_pad, L.rows_pad, static_cast<int>(L.naux_p),
-                                     kPairSlices, dig, 7, digb, 6, exps, sc, stream);
+  double* rowsq = reinterpret_cast<double*>(ws + L.off_rowsq);
+  const bool b254 = use_pe254(naux);
+  cudaError_t e = cudaSuccess;
+  if (b254) {
+    // per-row exponents and sums of squares, then the base-254 digits in both layouts
+    const int R = static_cast<int>(L.R);
+    ozk_init_kernel<<<(R + 255) / 256 + 1, 256, 0, stream>>>(sc.maxbits, R, sc.shift_range);
+    pe254_rowstats_kernel<<<static_cast<unsigned>((L.R + 7) / 8), 256, 0, stream>>>(
+        B, static_cast<int>(naux), L.R, sc.maxbits, rowsq);
+    ozk_exps_kernel<<<(R + 255) / 256, 256, 0, stream>>>(sc.maxbits, R, exps, sc.shift_range);
+    const long long tiles = (L.rows_pad / 32) * (L.naux_p / 32);
+    static int per_sm = 0;
+    if (per_sm == 0 &&
+        (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pe254_digits_kernel, 256, 0) != cudaSuccess ||
+         per_sm < 1))
+      per_sm = 1;
+    const long long g3 = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
+    pe254_digits_kernel<<<static_cast<unsigned>(g3), dim3(32, 8), 0, stream>>>(
+        B, static_cast<int>(naux), static_cast<int>(nvir), static_cast<int>(L.nv_pad), L.rows_pad,
+        static_cast<int>(L.naux_p), exps, dig, digb);
+    e = cudaGetLastError();
+  } else {
+    e = launch_split_tiled(B, naux, 1, static_cast<int>(L.R), static_cast<int>(naux), nvir, L.nv_pad,
+                           L.rows_pad, static_cast<int>(L.naux_p), kPairSlices, dig, 7, digb, 6,
+                           exps, sc, stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
   {
     const int g = pair_block(L, nocc);
@@ -557,22 +601,34 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   p.nR = static_cast<int>(ceil_div(nvir, 128));
   p.nC = static_cast<int>(ceil_div(nvir, 64));
   p.exps = exps;
+  p.rowsq = rowsq;
   p.eps_occ = eps_occ;
   p.eps_vir = eps_vir;
   p.partials = partials;
   p.status = status;
   p.timeout_ns = wait_timeout_ns();
 
-  constexpr int smem = kPairStages * PairCfg<kPairSlices>::STAGE_BYTES + 1024 + 256;
-  auto kern = pair_energy_kernel<kPairSlices, kPairStages>;
-  static bool attr_set[64] = {};
   const int dev = current_device();
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  if (b254) {
+    static bool attr_set[64] = {};
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(pair_energy254_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Pe254::SMEM);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    pair_energy254_kernel<<<grid, Pe254::THREADS, Pe254::SMEM, stream>>>(p);
+  } else {
+    constexpr int smem = kPairStages * PairCfg<kPairSlices>::STAGE_BYTES + 1024 + 256;
+    auto kern = pair_energy_kernel<kPairSlices, kPairStages>;
+    static bool attr_set[64] = {};
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    kern<<<grid, kPairThreads, smem, stream>>>(p);
   }
-  kern<<<grid, kPairThreads, smem, stream>>>(p);
   pair_energy_finish<<<1, 32, 0, stream>>>(partials, grid, energy);
   e = cudaGetLastError();
   return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "pair energy launch");

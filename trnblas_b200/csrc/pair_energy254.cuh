@@ -1,0 +1,468 @@
+// Fused DF-MP2 pair energy, base-254 digit form: 10 int8 slice products.
+//
+// Same energy, pair walk and work units as the 7-bit kernel of
+// pair_energy.cu (units of one pair (i, j), a 128-row block R of a and a
+// 64-column block C >= 2R of b; X = B_i[R] B_j[C]^T and Y = B_j[R] B_i[C]^T
+// in the same TMEM lanes and columns), with these changes:
+//
+// Digits. B is split per row (i, a) into KS = 4 balanced base-254 digits:
+// with e the frexp exponent of the row's max |B| and u = B * 127 * 2^-e
+// (exact in fp64, |u| < 127), d_0 = rint(u), then repeatedly
+// u = 254 (u - d_s), d_{s+1} = rint(u) (every step is exact in fp64 for fp32
+// B: each one drops a fractional bit); |d| <= 127 and
+//     B = 2^e / 127 (d_0 + d_1 / 254 + d_2 / 254^2 + d_3 / 254^3) + r,
+// |r| <= 2^e * 2.4e-10. T keeps the diagonals s + t <= 3 of the slice
+// products (10 products, 4 int32 accumulators per column):
+//     T_ab = 2^(e_ia + e_jb) / 127^2 * sum_{d <= 3} 254^-d S_d,
+// every S_d exact in int32 while 4 * 127^2 * naux < 2^31 (naux <= 33280).
+//
+// The truncation errors of different rows are independent, so they average
+// out in E, except on the diagonal elements T_aa = sum_P B_ia^2 of the pairs
+// i == j, where a digit multiplies itself and the dropped d_s d_t (s + t >= 4)
+// are squares: a positive bias of ~1e-9 relative on those elements (measured
+// on the GPU: 1.5e-9 on E for the single pair (0, 0) at nvir / naux =
+// 300 / 200). Those elements are taken instead from exact fp64 row sums of
+// squares, computed in the row-max pass. An fp64 emulation of the whole
+// arithmetic then puts E within 4e-12 .. 2e-11 (relative) of the fp64 energy
+// on that pair, at 5 / 37 / 45 and at 48 / 432 / 1152 (3 digits with
+// diagonals <= 2, 6 products, reach 1.1e-8 at 5 / 37 / 45: too few terms
+// average the truncation errors there).
+//
+// Epilogue in fp64. The diagonals are folded (smallest first), scaled by the
+// exact power of two and multiplied into the numerators in fp64; the common
+// factor 1 / 127^4 is applied once per thread.
+//
+// Pipeline. One stage holds a 64-wide K superslab of all 4 planes of the
+// 128-row A block (32 KB) and of the 64-row B block (16 KB), each ONE bulk
+// copy (the digits are stored in that image, `sblocked_offset`): about 640
+// cycles of the SM's copy engine against ~670 of MMA per stage. TMEM holds
+// two pass buffers of 4 x 64 columns (X in buffer 0, Y in buffer 1: all 512
+// columns), so the MMA runs the next pass while the epilogue folds the last.
+#pragma once
+
+#include "ozaki_split.cuh"
+
+namespace tb {
+
+// Superslab blocked digit layout: [K superslab of 2^sw_log2][row block of
+// 2^rb_log2 rows][plane][8-row group][16-byte K chunk][row in group (8)]
+// [16 bytes]. All planes of one row block of one superslab form one chunk;
+// inside a plane the K-major no-swizzle core matrices sit LBO = 128 bytes
+// apart along K and SBO = 2^sw_log2 * 8 bytes apart along the rows.
+__host__ __device__ __forceinline__ long long sblocked_offset(long long p, int k, int s, int slices,
+                                                              long long rows_pad, int rb_log2,
+                                                              int sw_log2) {
+  const long long ss = k >> sw_log2;
+  const int kk = k & ((1 << sw_log2) - 1);
+  const long long nblk = rows_pad >> rb_log2;
+  const long long blk = p >> rb_log2;
+  const long long grp = (p & ((1ll << rb_log2) - 1)) >> 3;
+  const long long plane = (ss * nblk + blk) * slices + s;
+  return (plane << (rb_log2 + sw_log2)) + (((grp << (sw_log2 - 4)) + (kk >> 4)) << 7) +
+         ((p & 7) << 4) + (kk & 15);
+}
+
+__host__ __device__ __forceinline__ long long sblocked_chunk(long long ss, long long blk, int slices,
+                                                             long long rows_pad, int rb_log2,
+                                                             int sw_log2) {
+  return ((ss * (rows_pad >> rb_log2) + blk) * slices) << (rb_log2 + sw_log2);
+}
+
+struct Pe254 {
+  static constexpr int KS = 4;    // digit planes
+  static constexpr int DMAX = 3;  // diagonals s + t <= DMAX are kept
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int SW_LOG2 = 6, SW = 1 << SW_LOG2;  // K per stage
+  static constexpr int A_PLANE = BM * SW, B_PLANE = BN * SW;
+  static constexpr int A_OFF = 0, B_OFF = KS * A_PLANE;
+  static constexpr int STAGE_BYTES = KS * (A_PLANE + B_PLANE);
+  static constexpr int STAGES = 4;
+  static constexpr int ACC_COLS = (DMAX + 1) * BN;  // one pass buffer
+  static constexpr int EPI_WARPS = 16;              // 4 per TMEM lane quarter, 16 columns each
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+  static constexpr long long MAX_NAUX = 33280;  // 4 * 127^2 * naux < 2^31, a multiple of 32
+  static_assert(2 * ACC_COLS <= 512, "two pass buffers in TMEM");
+};
+
+// Per-row statistics of B (R rows of naux fp32, contiguous): max |x| as IEEE
+// bits (for the exponent) and the fp64 sum of squares, one warp per row,
+// reduced in a fixed order (deterministic).
+__global__ void __launch_bounds__(256)
+    pe254_rowstats_kernel(const float* __restrict__ B, int naux, long long R,
+                          unsigned long long* __restrict__ maxbits, double* __restrict__ rowsq) {
+  const long long r = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const float* row = B + r * naux;
+  unsigned long long mb = 0;
+  double sq = 0.0;
+  int k = lane;
+  for (; k + 96 < naux; k += 128) {
+    const float x0 = __ldg(row + k), x1 = __ldg(row + k + 32), x2 = __ldg(row + k + 64),
+                x3 = __ldg(row + k + 96);
+    mb = umax64(umax64(mb, abs_bits(x0)), umax64(abs_bits(x1), umax64(abs_bits(x2), abs_bits(x3))));
+    sq = fma(static_cast<double>(x0), static_cast<double>(x0), sq);
+    sq = fma(static_cast<double>(x1), static_cast<double>(x1), sq);
+    sq = fma(static_cast<double>(x2), static_cast<double>(x2), sq);
+    sq = fma(static_cast<double>(x3), static_cast<double>(x3), sq);
+  }
+  for (; k < naux; k += 32) {
+    const float x = __ldg(row + k);
+    mb = umax64(mb, abs_bits(x));
+    sq = fma(static_cast<double>(x), static_cast<double>(x), sq);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mb = umax64(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  }
+  if (lane == 0) {
+    maxbits[r] = mb;
+    rowsq[r] = sq;
+  }
+}
+
+// Base-254 digits of B (nocc * nvir rows of naux fp32, row (i, a) at
+// i * nvir + a) into the superslab layout twice: 128-row blocks (digA, the A
+// operand) and 64-row blocks (digB); padded row p = i * nv_pad + a, zero for
+// a >= nvir and k >= naux. 32 x 32 tiles through a cp.async ring (persistent
+// grid), each thread 4 consecutive K of one row, one 32-bit store per plane
+// and layout.
+__global__ void __launch_bounds__(256)
+    pe254_digits_kernel(const float* __restrict__ B, int naux, int nvir, int nv_pad,
+                        long long rows_pad, int naux_p, const int* __restrict__ exps,
+                        int8_t* __restrict__ digA, int8_t* __restrict__ digB) {
+  __shared__ __align__(16) float tile[kOzBuf][32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y, t = ty * 32 + tx;
+  const int nslab = naux_p / 32;
+  const long long nrb = rows_pad / 32;
+  const long long total = nrb * nslab;
+  auto src_row = [&](long long p) -> long long {
+    const long long q = p / nv_pad, a = p - q * nv_pad;
+    return a < nvir ? q * nvir + a : -1;
+  };
+  auto issue = [&](long long tile_id, int buf) {
+    if (tile_id < total) {
+      const long long rb = tile_id / nslab;
+      const int k0 = static_cast<int>(tile_id - rb * nslab) * 32;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = ty + 8 * j;
+        const long long r = src_row(rb * 32 + i);
+        const int k = k0 + tx;
+        const bool ok = r >= 0 && k < naux;
+        cp_async_zfill<4>(&tile[buf][i][tx], ok ? B + r * naux + k : B, ok);
+      }
+    }
+    cp_async_commit();
+  };
+  const int crow = t >> 3, kq = (t & 7) * 4;
+  const long long G = gridDim.x;
+  long long tc = blockIdx.x, tl = blockIdx.x;
+#pragma unroll
+  for (int b = 0; b < kOzBuf - 1; ++b, tl += G) issue(tl, b);
+  const double M = 6755399441055744.0;  // 1.5 * 2^52: adding it rounds |u| < 2^51 to an integer
+  for (int it = 0; tc < total; tc += G, ++it) {
+    cp_async_wait<kOzBuf - 2>();
+    __syncthreads();
+    issue(tl, (it + kOzBuf - 1) % kOzBuf);
+    tl += G;
+    const int buf = it % kOzBuf;
+    const long long rb = tc / nslab;
+    const int k0 = static_cast<int>(tc - rb * nslab) * 32;
+    const long long p = rb * 32 + crow;
+    const long long r = src_row(p);
+    const double f = 127.0 * pow2d(r >= 0 ? -__ldg(exps + r) : 0);  // exact: |e| <= 149
+    double u[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) u[e] = static_cast<double>(tile[buf][crow][kq + e]) * f;  // exact
+    int8_t* outA = digA + sblocked_offset(p, k0 + kq, 0, Pe254::KS, rows_pad, 7, Pe254::SW_LOG2);
+    int8_t* outB = digB + sblocked_offset(p, k0 + kq, 0, Pe254::KS, rows_pad, 6, Pe254::SW_LOG2);
+#pragma unroll
+    for (int s = 0; s < Pe254::KS; ++s) {
+      int d[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const double tt = __dadd_rn(u[e], M);
+        d[e] = __double2loint(tt);
+        // remainder times 254, both exact (the remainder of an fp32 input
+        // keeps fewer than 32 significant bits)
+        u[e] = __dmul_rn(__dsub_rn(u[e], __dsub_rn(tt, M)), 254.0);
+      }
+      const uint32_t w = __byte_perm(__byte_perm(d[0], d[1], 0x0040), __byte_perm(d[2], d[3], 0x0040),
+                                     0x5410);
+      *reinterpret_cast<uint32_t*>(outA + s * Pe254::A_PLANE) = w;
+      *reinterpret_cast<uint32_t*>(outB + s * Pe254::B_PLANE) = w;
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// MMA issue for one stage: SW / 32 K steps of 32; at each, A-plane s against
+// the B planes 0 .. DMAX - s stacked along N, into diagonal columns s * BN ...
+// of the pass buffer (s = 0 initialises all of them on the pass's first step).
+template <int OFF>
+__device__ __forceinline__ void pe254_issue(uint64_t dA, uint64_t dB, uint32_t d_tmem, bool first) {
+  using C = Pe254;
+#pragma unroll
+  for (int kk = 0; kk < C::SW / 32; ++kk) {
+#pragma unroll
+    for (int s = 0; s <= C::DMAX; ++s) {
+      const int N = (C::DMAX + 1 - s) * C::BN;
+      mma_i8(d_tmem + s * C::BN, sdesc_add(dA, OFF + s * C::A_PLANE + kk * 256),
+             sdesc_add(dB, OFF + kk * 256), idesc(kAccS32, kFmtS8, kFmtS8, 0, 0, 128, N),
+             (first && kk == 0 && s == 0) ? 0u : 1u);
+    }
+  }
+}
+
+// MMA issuer over this CTA's stream of stages (units x 2 passes x num_kb),
+// unrolled over the pipeline stages (compile-time shared-memory offsets);
+// pass it uses TMEM buffer it & 1.
+__device__ __forceinline__ void pe254_mma_role(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
+                                               uint64_t* accf_bar, uint64_t* acce_bar,
+                                               uint32_t tmem_base, int num_kb, long long total,
+                                               const Abort& ab) {
+  using C = Pe254;
+  constexpr int STAGES = C::STAGES;
+  const uint32_t base = smem_u32(smem);
+  const uint64_t dA = sdesc_kmajor_noswz(base + C::A_OFF, 128, C::SW * 8);
+  const uint64_t dB = sdesc_kmajor_noswz(base + C::B_OFF, 128, C::SW * 8);
+  uint32_t phase = 0;
+  int it = 0;   // passes started
+  int kbp = 0;  // stage within the pass
+  uint32_t d_tmem = tmem_base;
+  bool stop = false;
+  for (long long g = 0; g < total && !stop; g += STAGES) {
+    static_for<0, STAGES>([&](auto sc) {
+      constexpr int S = decltype(sc)::value;
+      if (stop || g + S >= total) return;
+      if (kbp == 0) {
+        const int buf = it & 1;
+        if (!mbar_wait(&acce_bar[buf], ((it >> 1) & 1) ^ 1u, ab, kTimeoutAccEmpty)) {
+          stop = true;
+          return;
+        }
+        tc_fence_after();
+        d_tmem = tmem_base + buf * C::ACC_COLS;
+      }
+      if (!mbar_wait(&full_bar[S], phase, ab, kTimeoutFull)) {
+        stop = true;
+        return;
+      }
+      tc_fence_after();
+      pe254_issue<S * C::STAGE_BYTES>(dA, dB, d_tmem, kbp == 0);
+      tc_commit(&empty_bar[S]);
+      if (++kbp == num_kb) {
+        tc_commit(&accf_bar[it & 1]);
+        kbp = 0;
+        ++it;
+      }
+    });
+    phase ^= 1u;
+  }
+}
+
+// Block: warp 0 producer, warp 1 MMA issuer and TMEM owner, warps 2..17
+// epilogue (four per TMEM lane quarter, 16 columns of the 64 each).
+__global__ void __launch_bounds__(Pe254::THREADS, 1) pair_energy254_kernel(const PairParams p) {
+  using C = Pe254;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint64_t* drain_bar = acce_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  double* red = reinterpret_cast<double*>(smem + STAGES * C::STAGE_BYTES + 256);  // [EPI_WARPS]
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier block");
+  static_assert(256 + 8 * C::EPI_WARPS <= C::BAR_BYTES, "reduction slots");
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Abort ab{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], C::EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    for (int w = 0; w < C::EPI_WARPS; ++w) red[w] = 0.0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = p.naux_p / C::SW;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool aborted = false;
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      int i, j, R, Cb;
+      unit_of(p, u, i, j, R, Cb);
+      const long long ri = static_cast<long long>(i) * p.nv_pad;
+      const long long rj = static_cast<long long>(j) * p.nv_pad;
+      for (int pass = 0; pass < 2 && !aborted; ++pass) {
+        const long long ra = (pass == 0 ? ri : rj) + 128 * R;  // A rows: B_i[R] then B_j[R]
+        const long long rb = (pass == 0 ? rj : ri) + 64 * Cb;  // B rows: B_j[C] then B_i[C]
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
+            aborted = true;
+            break;
+          }
+          uint8_t* st = smem + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          bulk_load(st + C::A_OFF,
+                    p.digA + sblocked_chunk(kb, ra >> 7, C::KS, p.rows_pad, 7, C::SW_LOG2),
+                    C::KS * C::A_PLANE, &full_bar[stage]);
+          bulk_load(st + C::B_OFF,
+                    p.digB + sblocked_chunk(kb, rb >> 6, C::KS, p.rows_pad, 6, C::SW_LOG2),
+                    C::KS * C::B_PLANE, &full_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    if (aborted || ab.raised()) {
+      int s = stage;
+      uint32_t ph = phase;
+      for (int k = 0; k < STAGES; ++k) {
+        if (s == 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        } else {
+          --s;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], ph))
+          if (globaltimer_ns() - t0 > 50000000ull) break;
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const long long my_units =
+        p.num_units > blockIdx.x ? (p.num_units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    pe254_mma_role(smem, full_bar, empty_bar, accf_bar, acce_bar, tmem_base, num_kb,
+                   my_units * 2 * num_kb, ab);
+    tc_commit(drain_bar);
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(drain_bar, 0)) {
+      if (globaltimer_ns() - t0 > 100000000ull) {
+        ab.raise(kTimeoutDrain);
+        break;
+      }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    constexpr int NCOL = C::BN / (C::EPI_WARPS / 4);  // 16 columns per warp
+    static_assert(NCOL == 16, "one 16-column TMEM load per diagonal");
+    const int q = warp & 3;
+    const int col0 = NCOL * ((warp - 2) / 4);
+    const int aloc = 32 * q + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + col0;
+    const double c1 = 1.0 / 254.0, c2 = 1.0 / 64516.0, c3 = 1.0 / 16387064.0;
+    double acc = 0.0;
+    int it = 0;
+    bool aborted = false;
+    for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      double xt[NCOL], yt[NCOL];
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass, ++it) {
+        if (!mbar_wait_warp(&accf_bar[pass], (it >> 1) & 1, ab, kTimeoutAccFull)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v0[16], v1[16], v2[16], v3[16];
+        const uint32_t col = lane_base + pass * C::ACC_COLS;
+        tmem_ld16(col, v0);
+        tmem_ld16(col + C::BN, v1);
+        tmem_ld16(col + 2 * C::BN, v2);
+        tmem_ld16(col + 3 * C::BN, v3);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce_bar[pass]);  // the buffer is free for the pass after next
+#pragma unroll
+        for (int jj = 0; jj < NCOL; ++jj) {
+          // smallest diagonal first: S_3 / 254^3 + S_2 / 254^2 + S_1 / 254 + S_0
+          double t = static_cast<double>(static_cast<int>(v3[jj])) * c3;
+          t = fma(static_cast<double>(static_cast<int>(v2[jj])), c2, t);
+          t = fma(static_cast<double>(static_cast<int>(v1[jj])), c1, t);
+          t += static_cast<double>(static_cast<int>(v0[jj]));
+          if (pass == 0)
+            xt[jj] = t;
+          else
+            yt[jj] = t;
+        }
+      }
+      if (aborted) break;
+      int i, j, R, Cb;
+      unit_of(p, u, i, j, R, Cb);
+      const int a = 128 * R + aloc;
+      // lane mode: 2 = both ordered pairs, 1 = (a, b) once, 0 = skip
+      int mode = 2;
+      if (Cb == 2 * R + 1) mode = (aloc < 64) ? 2 : 1;
+      if (Cb == 2 * R) mode = (aloc < 64) ? 1 : 0;
+      if (a >= p.nvir) mode = 0;
+      double usum = 0.0;
+      if (mode) {
+        const int eia = p.exps[i * p.nvir + a], eja = p.exps[j * p.nvir + a];
+        const double da = (static_cast<double>(p.eps_occ[i]) + static_cast<double>(p.eps_occ[j])) -
+                          static_cast<double>(p.eps_vir[a]);
+        const int b0 = 64 * Cb + col0;
+#pragma unroll
+        for (int jj = 0; jj < NCOL; ++jj) {
+          const int b = b0 + jj;
+          if (b < p.nvir) {
+            double X = xt[jj] * pow2d(eia + p.exps[j * p.nvir + b]);
+            double Y = yt[jj] * pow2d(eja + p.exps[i * p.nvir + b]);
+            if (i == j && b == a) X = Y = p.rowsq[i * p.nvir + a] * 16129.0;  // exact T_aa * 127^2
+            const double den = da - static_cast<double>(p.eps_vir[b]);
+            double f = X * (2.0 * X - Y);
+            if (mode == 2) f = fma(Y, 2.0 * Y - X, f);
+            usum += f / den;
+          }
+        }
+      }
+      acc += ((i == j) ? 1.0 : 2.0) * usum;
+    }
+    acc *= 1.0 / 260144641.0;  // 127^-4: T = 2^(e + e') / 127^2 * fold
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) red[warp - 2] = acc;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double part = 0.0;
+    for (int w = 0; w < C::EPI_WARPS; ++w) part += red[w];  // fixed order
+    p.partials[blockIdx.x] = part;
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace tb

@@ -257,8 +257,26 @@ TRAFFIC = {
     "syrk": 528911104,             # profiles/gemm_syrk_4096.md
     "syrk_bf16": 34854912,         # profiles/gemm_syrk_bf16_4096.md
     "gemm_fp64": 2161969960,       # profiles/ozaki_fp64_4096.md (the int8 GEMM kernel)
-    "pair3": 2699185008,           # profiles/pair_energy_pair3.md
 }
+
+
+# naux above which the pair energy runs its 7-bit form (15 int8 products per
+# 64-column block of T) instead of the base-254 form (10 products)
+PAIR_B254_MAX_NAUX = 33280
+
+
+def pair_int8_ops(npairs: int, nvir: int, naux: int) -> float:
+    """int8 ops (2 per multiply-add) the fused pair-energy kernel issues for
+    `npairs` pairs: units (128 rows of a x 64 columns of b, C >= 2R) x 2
+    passes x the summed MMA N of one K step (10 or 15 products of 64
+    columns) x 128 rows x the padded naux."""
+    nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
+    upp = sum(max(0, nC - 2 * r) for r in range(nR))
+    if naux <= PAIR_B254_MAX_NAUX:
+        prods, naux_p = 10, math.ceil(naux / 64) * 64
+    else:
+        prods, naux_p = 15, math.ceil(naux / 32) * 32
+    return npairs * upp * 2 * prods * 64 * 128 * naux_p * 2.0
 
 
 def kernel_avg_ms(events):
@@ -280,6 +298,9 @@ def pair_metric(nocc: int, nvir: int, naux: int) -> str:
 # The pair-energy block of the default line (config 5b): its own step counts,
 # reported in the block (a config-5b step takes seconds on one GPU).
 PAIR5_STEPS, PAIR5_WARMUP = 5, 3
+# The fp32 GEMM block of the default line (config 5a in fp32, ~0.3 s a step
+# on one GPU).
+FP32_STEPS, FP32_WARMUP = 5, 3
 
 
 # ── CPU baseline (the reference's CPU route, restated) ──────────────────────
@@ -541,11 +562,7 @@ def run_pair(args, rank, world, gpu, nocc, nvir, naux, steps=None, warmup=None):
     e_ev.record()
     torch.cuda.synchronize()
     kern_ms = s_ev.elapsed_time(e_ev)
-    # int8 pipe: units x 2 passes x (sum of MMA N) x 128 rows x naux_p x 2 ops
-    nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
-    upp = sum(max(0, nC - 2 * r) for r in range(nR))
-    naux_p = math.ceil(naux / 32) * 32
-    int8_ops = npairs * upp * 2 * (5 * 64 + 4 * 64 + 3 * 64 + 2 * 64 + 64) * 128 * naux_p * 2.0
+    int8_ops = pair_int8_ops(npairs, nvir, naux)
     # int8 dense rate = 2 x the bf16 dense rate (4.5 POPS vs 2.25 PFLOP/s nominal), both
     # counted as 2 ops per multiply-add; the burst bf16 figure for a launch under a second
     # (full clocks), the sustained one for longer launches (power-capped clocks)
@@ -605,6 +622,7 @@ def main():
                              "pair5x4", "dfmp2", "gemm_fp64", "batched", "syrk", "batched_bf16",
                              "syrk_bf16", "gemm1024"])
     ap.add_argument("--no-pair", action="store_true", help="skip the pair-energy block of the default line")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 GEMM block of the default line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -635,8 +653,18 @@ def run_ours(args, rank, world, gpu):
             line["pair_energy"] = {"metric": pair_metric(96, 2208, 6912), "value": pe["ms_per_step"],
                                    "unit": "ms", "higher_is_better": False,
                                    "steps": min(args.steps, PAIR5_STEPS), "warmup": PAIR5_WARMUP, **pe}
+        if args.workload == "spmd" and not args.no_fp32:
+            # config 5a in fp32 (3xTF32), the reference's working precision:
+            # its own block, step counts and metric
+            sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, FP32_STEPS),
+                                        "warmup": FP32_WARMUP})
+            blk = run_gemm_spmd(sub, rank, world, gpu, torch.float32)
+            blk.pop("vs_baseline", None)
+            line["gemm_fp32"] = blk
         if rank == 0:
             line["cpu_baseline"] = cpu_baseline_gemm(dt) if world == 1 else None
+            if "gemm_fp32" in line and world == 1:
+                line["gemm_fp32"]["cpu_baseline"] = cpu_baseline_gemm(torch.float32)
         return line
     if args.workload == "dfmp2":
         return run_dfmp2(args, rank, world, gpu)
@@ -647,7 +675,7 @@ def run_ours(args, rank, world, gpu):
             "metric": pair_metric(*dims),
             "value": r["ms_per_step"], "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8 (5 Ozaki slices, exact int32) + fp64 reduction",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 (base-254 digit slices, exact int32) + fp64 epilogue",
             "data": "synthetic (benchmark recipe, device generator)",
             "config": {"workload": args.workload, **r["config"]},
             "roofline": {"bound": "tensor", "achieved": r["int8_tops_achieved"], "peak": r["int8_peak_tops"],
@@ -713,10 +741,8 @@ def run_dfmp2(args, rank, world, gpu):
     flops = (2.0 * nbasis * nbasis * nocc * naux + 2.0 * nocc * nvir * nbasis * naux
              + 2.0 * nocc * nvir * naux * naux + nocc * (nocc + 1) / 2 * 2.0 * nvir * nvir * naux)
     # dominant stage: the fused pair energy (int8 pipe), timed by the stage clock
-    nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
-    upp = sum(max(0, nC - 2 * r) for r in range(nR))
     npairs_rank = (lambda pr: pr[1] - pr[0])(__import__("trnblas_b200").energy.pair_ranges(nocc, world)[rank])
-    int8_ops = npairs_rank * upp * 2 * (5 * 64 + 4 * 64 + 3 * 64 + 2 * 64 + 64) * 128 * math.ceil(naux / 32) * 32 * 2.0
+    int8_ops = pair_int8_ops(npairs_rank, nvir, naux)
     pk, src = peaks()
     e_ms = t.get("energy", float("nan")) * 1e3
     ach = int8_ops / (e_ms / 1e3) / 1e12
@@ -724,7 +750,7 @@ def run_dfmp2(args, rank, world, gpu):
         "metric": f"DF-MP2 energy ms ({nbasis}/{nocc}/{naux}, end to end)",
         "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-        "dtype": "fp32 (3xTF32) GEMMs + int8 (5 Ozaki slices) pair energy",
+        "dtype": "fp32 (3xTF32) GEMMs + int8 (base-254 digit slices) pair energy",
         "data": "synthetic (examples/df_mp2 distributions, device generator)",
         "config": {"workload": "dfmp2", "nbasis": nbasis, "nocc": nocc, "naux": naux,
                    "sharding": "integral rows by bytes, pairs by count"},
@@ -1014,13 +1040,20 @@ def reference_arm(args, world):
     v = round(rate / 1e12, 4)
     cb = {"unit": "TFLOP/s", "cores": threads, "kind": "port",
           "sample": f"{rows} x {n} rows of the {n}^3 product per step, {dt} (torch CPU matmul: the reference's host route)"}
-    extra = None
+    extra = {}
     if wl == "spmd" and not args.no_pair:
         ms, th, sample = cpu_pair_sample(96, 2208, 6912, budget_s=8.0)
-        extra = {"pair_energy": {"metric": pair_metric(96, 2208, 6912), "value": round(ms, 1), "unit": "ms",
-                                 "higher_is_better": False, "steps": 1, "warmup": 0,
-                                 "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port",
-                                                  "sample": sample}}}
+        extra["pair_energy"] = {"metric": pair_metric(96, 2208, 6912), "value": round(ms, 1), "unit": "ms",
+                                "higher_is_better": False, "steps": 1, "warmup": 0,
+                                "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": th, "kind": "port",
+                                                 "sample": sample}}
+    if wl == "spmd" and not args.no_fp32:
+        del A, B
+        v32, th, sample = cpu_gemm_sample(n, torch.float32, budget_s=8.0)
+        extra["gemm_fp32"] = {"metric": gemm_metric(n, torch.float32), "value": round(v32, 4), "unit": "TFLOP/s",
+                              "higher_is_better": True, "steps": 1, "warmup": 1,
+                              "cpu_baseline": {"value": round(v32, 4), "unit": "TFLOP/s", "cores": th, "kind": "port",
+                                               "sample": sample + " (torch CPU matmul: the reference's host route)"}}
     return _ref_line(args, world, gemm_metric(n, dt), "TFLOP/s", True, v, sec * 1e3, cb, extra)
 
 

@@ -73,6 +73,16 @@ def test_both_arms_name_the_same_metric(bench):
     assert '"metric": gemm_metric(n, dtype)' in ours and "gemm_metric(n, dt)" in ref
     assert "pair_metric(96, 2208, 6912)" in inspect.getsource(bench.run_ours)
     assert "pair_metric(96, 2208, 6912)" in ref
+    assert "gemm_metric(n, torch.float32)" in ref and "torch.float32)" in inspect.getsource(bench.run_ours)
+
+
+def test_pair_int8_ops_follow_the_kernel_form(bench):
+    """Config 3 (48/432/1152) runs the base-254 form: 10 products per K step
+    of each 128 x 64 unit; past naux 33280 the 7-bit form's 15."""
+    ops = bench.pair_int8_ops(1176, 432, 1152)
+    units = 7 + 5 + 3 + 1
+    assert ops == 1176 * units * 2 * 10 * 64 * 128 * 1152 * 2.0
+    assert bench.pair_int8_ops(1, 40, 33281) == 1 * 1 * 2 * 15 * 64 * 128 * 33312 * 2.0
     assert "read_traffic" not in (ROOT / "bench.py").read_text()
 
 

@@ -97,6 +97,48 @@ TRNBLAS_API int trnblas_gemm_f32_noalloc(int64_t M, int64_t N, int64_t K, float 
                              float beta, const float* C, int64_t ldc, float* D, int64_t ldd,
                              void* stream);
 
+/*
+ * bf16 / fp16 trnblas_gemm (no workspace) whose operands arrive while it runs:
+ * rows [s * shard_rows, (s + 1) * shard_rows) of op(A) may be read once
+ * ready[s] has reached `epoch` (wrap-safe), batch entry b of op(B) once
+ * ready[ready_b0 + b] has; the tile walk starts at row rot_rows of op(A) and
+ * batch entry rot_b (so tiles whose operands are already in place go
+ * first). The flags are device ints written by the caller's copies, e.g.
+ * trnblas_copy_async followed by trnblas_stream_signal on a copy stream.
+ * Every wait is bounded (the status word records a timeout). shard_rows and
+ * rot_rows are multiples of 256. Replaces the gather-then-multiply step of
+ * the reference's 2-D SPMD GEMM primitives (trnblas/parallel.py:81-120,
+ * all_gather_rows + gemm_row/col_parallel) for trnblas_b200.parallel.gemm_2d.
+ */
+TRNBLAS_API int trnblas_gemm_ready(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                       const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                       int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                       int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
+                       const int* ready, int epoch, int64_t shard_rows, int ready_b0,
+                       int64_t rot_rows, int rot_b, void* stream);
+
+/*
+ * Device memory of another process of this node (one process per GPU):
+ * trnblas_ipc_export writes the 64-byte CUDA IPC handle of the allocation
+ * holding `ptr` and ptr's offset in it; trnblas_ipc_open maps a peer's
+ * allocation (cached per device and handle, at most 64 mappings) and returns
+ * the peer pointer; trnblas_ipc_close_all unmaps them. Legacy CUDA IPC (no
+ * multicast object). The all-gather step of the reference's SPMD GEMM
+ * (trnblas/parallel.py:81-86, all_gather_rows) becomes copies from these
+ * pointers.
+ */
+TRNBLAS_API int trnblas_ipc_export(const void* ptr, void* handle, int64_t* offset);
+TRNBLAS_API int trnblas_ipc_open(const void* handle, int64_t offset, void** ptr);
+TRNBLAS_API int trnblas_ipc_close_all(void);
+
+/* One device-to-device cudaMemcpyAsync (a peer pointer as source: the copy
+ * engines pull over NVLink, no SM is used). */
+TRNBLAS_API int trnblas_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+/* Store `value` to the device int *flag once the stream's earlier work is
+ * done and visible (a stream memory operation). */
+TRNBLAS_API int trnblas_stream_signal(int* flag, int value, void* stream);
+
 /* Bytes of workspace trnblas_syrk needs (0 for bf16/fp16). */
 TRNBLAS_API size_t trnblas_syrk_workspace_size(int dtype, int64_t n, int64_t k);
 

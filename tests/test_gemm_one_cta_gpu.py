@@ -1,7 +1,7 @@
-"""The CTA-pair GEMM kernel (tcgen05 cta_group::2, 256 x 256 tiles), which
-TRNBLAS_B200_GEMM_PAIR=1 selects for 16-bit GEMMs, against fp64 products:
-K-major and MN-major operands, ragged edges (including a tile whose second
-CTA's rows lie past M), a batched call and a long K with the wave
+"""The one-CTA GEMM kernel, which TRNBLAS_B200_GEMM_PAIR=0 selects for 16-bit
+GEMMs in place of the default CTA-pair kernel (tcgen05 cta_group::2, 256 x 256
+tiles; covered by test_gemm_gpu.py), against fp64 products: K-major and
+MN-major operands, ragged edges, a batched call and a long K with the wave
 synchronisation. The selection is read once per process, so the products run
 in a child process."""
 
@@ -44,8 +44,8 @@ print(json.dumps(out))
 """
 
 
-def test_pair_kernel_matches_fp64():
-    env = dict(os.environ, TRNBLAS_B200_GEMM_PAIR="1", PYTHONPATH=str(ROOT))
+def test_one_cta_kernel_matches_fp64():
+    env = dict(os.environ, TRNBLAS_B200_GEMM_PAIR="0", PYTHONPATH=str(ROOT))
     r = subprocess.run([sys.executable, "-c", CHILD], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     res = json.loads(r.stdout.strip().splitlines()[-1])

@@ -76,11 +76,11 @@ def test_host_inputs_and_errors():
     assert float(energy.pair_range_energy(B, eo, ev, 4, 4)) == 0.0
 
 
-@pytest.mark.parametrize("naux", [33280, 33281])
-def test_naux_limit_of_each_form(naux):
-    """naux up to 33280 runs the base-254 form (10 int8 products, exact int32
-    while 4 * 127^2 * naux < 2^31); above it the 7-bit form (15 products).
-    Both sides of the limit against the fp64 oracle."""
+@pytest.mark.parametrize("naux", [33280, 33281, 70000])
+def test_naux_chunks(naux):
+    """The int32 slice sums are exact for 4 * 127^2 * naux < 2^31 (naux up to
+    33280); longer naux runs as chunks of K whose folds are summed in fp64:
+    one, two and three chunks against the fp64 oracle."""
     B, eo, ev = PE.make_inputs(2, 40, naux, 12)
     Bd, eod, evd = _dev(B, eo, ev)
     ref = PE.chunked_energy(B.numpy(), eo.numpy(), ev.numpy())

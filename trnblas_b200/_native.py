@@ -37,6 +37,16 @@ _SIGNATURES = {
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
          _i64, _p, _i64, _i64, _p, _sz, _p],
     ),
+    "trnblas_gemm_ready": (
+        _i,
+        [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
+         _i64, _p, _i64, _i64, _p, _i, _i64, _i, _i64, _i, _p],
+    ),
+    "trnblas_ipc_export": (_i, [_p, _p, ctypes.POINTER(_i64)]),
+    "trnblas_ipc_open": (_i, [_p, _i64, ctypes.POINTER(_p)]),
+    "trnblas_ipc_close_all": (_i, []),
+    "trnblas_copy_async": (_i, [_p, _p, _sz, _p]),
+    "trnblas_stream_signal": (_i, [_p, _i, _p]),
     "trnblas_gemm_f32_noalloc": (
         _i, [_i64, _i64, _i64, _f, _p, _i64, _i, _p, _i64, _i, _f, _p, _i64, _p, _i64, _p]
     ),

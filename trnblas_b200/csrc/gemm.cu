@@ -195,7 +195,8 @@ int group_m_override() {
 // Soft tile-wave synchronisation (soft_wave_wait) for long K loops with at
 // least two waves of tiles. Measured on a 32768^3 bf16 product under the 1 kW
 // power cap (one-CTA kernel, band of 16 row tiles): DRAM reads per launch
-// 144 -> 69 GB; the same box went 1145 -> 1209 TFLOP/s.
+// 144 -> 69 GB; the same box went 1145 -> 1209 TFLOP/s (pair kernel:
+// 912 -> 1347 TFLOP/s on another box).
 // TRNBLAS_B200_GEMM_WAVESYNC = 0 / 1 overrides the default (on).
 bool use_wave_sync(long long K, long long tiles, long long grid) {
   static const int mode = [] {
@@ -271,18 +272,18 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, 
 bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBLAS_F16; }
 
 // CTA-pair tiles (256 x 256) for 16-bit GEMMs with at least two 128-row and
-// two 128-column blocks, when TRNBLAS_B200_GEMM_PAIR=1. Not the default: the
-// pair kernel keeps the tensor pipe busier per clock (8192^3: 92 % of cycles
-// against 76 %, 1439 against 1323 TFLOP/s at full clock), but it spends more
-// energy per flop, so under the 1 kW power cap of a sustained run its clock
-// falls further and it finishes later (32768^3: 0.89-0.98 TFLOP per joule
-// against 1.19-1.34 for the one-CTA kernel, measured on the same box).
+// two 128-column blocks (TRNBLAS_B200_GEMM_PAIR=0 keeps the one-CTA kernel).
+// Measured at 32768^3 bf16 under the 1 kW power cap, same box: pair kernel
+// with the wave synchronisation 1347 TFLOP/s (52.6 J a product), one-CTA
+// kernel 1248 TFLOP/s (52.5-58.7 J). Without the wave synchronisation the
+// pair kernel's tiles drift apart and re-read 246 GB from DRAM per product,
+// and it lost (912 against 1130 TFLOP/s).
 bool use_pair_gemm(long long M, long long N) {
   static const int mode = [] {
     const char* s = std::getenv("TRNBLAS_B200_GEMM_PAIR");
-    return (s && *s) ? std::atoi(s) : 0;
+    return (s && *s) ? std::atoi(s) : 1;
   }();
-  return mode == 1 && M > 128 && N > 128;
+  return mode != 0 && M > 128 && N > 128;
 }
 
 // Bytes of one fp32 split plane (R x Kp) for `nb` batch entries, 256-aligned.
@@ -373,11 +374,21 @@ size_t trnblas_gemm_workspace_size(int dtype, int64_t batch, int64_t M, int64_t 
   return 2 * plane_bytes(na, M, K) + 2 * plane_bytes(nbb, N, K);
 }
 
-int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
-                 const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
-                 int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
-                 int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
-                 void* workspace, size_t workspace_bytes, void* stream_) {
+// Operands that arrive while the GEMM runs (trnblas_gemm_ready).
+struct ReadySpec {
+  const int* flags;
+  int epoch;
+  long long shard_rows;  // rows of op(A) per flag
+  int b0;                // flags[b0 + b]: batch entry b of op(B)
+  long long rot_rows;    // the walk starts at this row of op(A) ...
+  int rot_b;             // ... and at this batch entry
+};
+
+static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                     const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                     int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                     int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
+                     void* workspace, size_t workspace_bytes, void* stream_, const ReadySpec* rs) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (int rc = check_dims(batch, M, N, K)) return rc;
   if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
@@ -445,6 +456,19 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   const long long nba = a_b ? batch : 1, nbb = b_b ? batch : 1;
 
   CUtensorMap ma0, ma1, mb0, mb1;
+  if (rs) {
+    if (dtype == TRNBLAS_F32 || !rs->flags || rs->shard_rows <= 0 || rs->shard_rows % 256 ||
+        rs->rot_rows < 0 || rs->rot_rows % 256 || rs->rot_rows >= M || rs->rot_b < 0 ||
+        rs->rot_b >= batch || rs->b0 < 0) {
+      set_error("trnblas_gemm_ready: bf16/fp16 only; flags, shard_rows and rot_rows (multiples of "
+                "256) and rot_b < batch required");
+      return TRNBLAS_ERR_ARG;
+    }
+    p.ready = rs->flags;
+    p.ready_epoch = rs->epoch;
+    p.ready_b0 = rs->b0;
+    p.rot_b = rs->rot_b;
+  }
   if (dtype == TRNBLAS_F32) {
     const size_t need = trnblas_gemm_workspace_size(dtype, batch, M, N, K, strideA, strideB);
     if (!workspace || workspace_bytes < need) {
@@ -500,6 +524,10 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
     p.tiles_m = static_cast<int>(ceil_div(M, 256));
     p.tiles_n = static_cast<int>(ceil_div(N, 256));
     p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+    if (rs) {
+      p.shard_tiles_m = static_cast<int>(rs->shard_rows / 256);
+      p.rot_m = static_cast<int>(rs->rot_rows / 256) % p.tiles_m;
+    }
     return launch_gemm_pair<6>(ma0, mb0, p, stream);
   }
   const int bn = pick_bn(batch, M, N);
@@ -511,8 +539,33 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   p.tiles_m = static_cast<int>(ceil_div(M, 128));
   p.tiles_n = static_cast<int>(ceil_div(N, bn));
   p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+  if (rs) {
+    p.shard_tiles_m = static_cast<int>(rs->shard_rows / 128);
+    p.rot_m = static_cast<int>(rs->rot_rows / 128) % p.tiles_m;
+  }
   if (bn == 256) return launch_gemm<kF16, 256, 4>(ma0, ma0, mb0, mb0, p, stream);
   return launch_gemm<kF16, 128, 6>(ma0, ma0, mb0, mb0, p, stream);
+}
+
+int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                 const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                 int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                 int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_impl(dtype, batch, M, N, K, alpha, A, lda, strideA, transA, B, ldb, strideB, transB,
+                   beta, C, ldc, strideC, D, ldd, strideD, workspace, workspace_bytes, stream,
+                   nullptr);
+}
+
+int trnblas_gemm_ready(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                       const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                       int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                       int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
+                       const int* ready, int epoch, int64_t shard_rows, int ready_b0,
+                       int64_t rot_rows, int rot_b, void* stream) {
+  const ReadySpec rs{ready, epoch, shard_rows, ready_b0, rot_rows, rot_b};
+  return gemm_impl(dtype, batch, M, N, K, alpha, A, lda, strideA, transA, B, ldb, strideB, transB,
+                   beta, C, ldc, strideC, D, ldd, strideD, nullptr, 0, stream, &rs);
 }
 
 size_t trnblas_syrk_workspace_size(int dtype, int64_t n, int64_t k) {

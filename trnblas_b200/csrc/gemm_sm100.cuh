@@ -59,7 +59,40 @@ struct GemmParams {
   int* status;
   unsigned long long timeout_ns;
   int* wave_ctr;  // tile-wave synchronisation counter (nullptr: none)
+  // Operands that arrive while the kernel runs (the SPMD GEMM's shards, copied
+  // in by the copy engines): before loading a tile the producer waits until
+  // ready[row tile / shard_tiles_m] and ready[ready_b0 + batch index] reach
+  // ready_epoch. The walk is rotated by rot_m row tiles and rot_b batch
+  // entries so that the tiles of the shards already in place come first.
+  const int* ready;  // nullptr: operands resident
+  int ready_epoch;
+  int shard_tiles_m, ready_b0;
+  int rot_m, rot_b;
 };
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait (bounded) until *flag has reached `epoch` (wrap-safe comparison); the
+// proxy fence orders the TMA loads that follow after the flag's data.
+__device__ __forceinline__ bool wait_ready(const int* flag, int epoch, const Abort& ab) {
+  if (ld_acquire_gpu(flag) - epoch < 0) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_gpu(flag) - epoch < 0) {
+      if (ab.raised()) return false;
+      if (globaltimer_ns() - t0 > ab.timeout_ns) {
+        ab.raise(kTimeoutAux);
+        return false;
+      }
+      __nanosleep(256);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 
 // Soft wave barrier of the persistent tile walk: the producer waits until
 // every CTA has issued the loads of its previous tile (`target` arrivals on
@@ -224,6 +257,10 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz,
   const int rr = r - g * band;
   mb = first_m + rr % gsz;
   nb = rr / gsz;
+  if (p.ready) {
+    bz = (bz + p.rot_b) % p.batch;
+    mb = (mb + p.rot_m) % p.tiles_m;
+  }
 }
 
 __device__ __forceinline__ float load_c(const void* C, int out_kind, long long idx) {
@@ -465,6 +502,11 @@ __global__ void __launch_bounds__(192, 1)
         soft_wave_wait(p.wave_ctr, wave * static_cast<int>(gridDim.x), 100000ull);
       int bz, mb, nb;
       decode_tile(p, t, bz, mb, nb);
+      if (p.ready && (!wait_ready(p.ready + mb / p.shard_tiles_m, p.ready_epoch, ab) ||
+                      !wait_ready(p.ready + p.ready_b0 + bz, p.ready_epoch, ab))) {
+        aborted = true;
+        break;
+      }
       const int m0 = mb * BM;
       const int n0 = nb * ((p.mode == kModeSyrk) ? BM : BN);
       const int za = p.a_batched ? bz : 0;

@@ -166,6 +166,11 @@ __global__ void __launch_bounds__(192, 1)
         soft_wave_wait(p.wave_ctr, wave * static_cast<int>(gridDim.x), 100000ull);
       int bz, mb, nb;
       decode_tile(p, t, bz, mb, nb);
+      if (p.ready && (!wait_ready(p.ready + mb / p.shard_tiles_m, p.ready_epoch, ab) ||
+                      !wait_ready(p.ready + p.ready_b0 + bz, p.ready_epoch, ab))) {
+        aborted = true;
+        break;
+      }
       const int m0 = mb * Cfg::BM + Cfg::HM * static_cast<int>(rank);
       const int n0 = nb * Cfg::BN + Cfg::HN * static_cast<int>(rank);
       const int za = p.a_batched ? bz : 0;

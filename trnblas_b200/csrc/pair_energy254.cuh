@@ -1,9 +1,9 @@
 // Fused DF-MP2 pair energy, base-254 digit form: 10 int8 slice products.
 //
-// Same energy, pair walk and work units as the 7-bit kernel of
-// pair_energy.cu (units of one pair (i, j), a 128-row block R of a and a
-// 64-column block C >= 2R of b; X = B_i[R] B_j[C]^T and Y = B_j[R] B_i[C]^T
-// in the same TMEM lanes and columns), with these changes:
+// The pair walk and work units are those of pair_energy.cu (units of one
+// pair (i, j), a 128-row block R of a and a 64-column block C >= 2R of b;
+// X = B_i[R] B_j[C]^T and Y = B_j[R] B_i[C]^T in the same TMEM lanes and
+// columns).
 //
 // Digits. B is split per row (i, a) into KS = 4 balanced base-254 digits:
 // with e the frexp exponent of the row's max |B| and u = B * 127 * 2^-e
@@ -15,6 +15,9 @@
 // products (10 products, 4 int32 accumulators per column):
 //     T_ab = 2^(e_ia + e_jb) / 127^2 * sum_{d <= 3} 254^-d S_d,
 // every S_d exact in int32 while 4 * 127^2 * naux < 2^31 (naux <= 33280).
+// Longer naux runs each X and Y pass as chunks of at most 33280 (520 stages)
+// of K, each a TMEM accumulation of its own whose fold the epilogue adds in
+// fp64.
 //
 // The truncation errors of different rows are independent, so they average
 // out in E, except on the diagonal elements T_aa = sum_P B_ia^2 of the pairs
@@ -82,7 +85,8 @@ struct Pe254 {
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
-  static constexpr long long MAX_NAUX = 33280;  // 4 * 127^2 * naux < 2^31, a multiple of 32
+  static constexpr long long CHUNK_NAUX = 33280;  // 4 * 127^2 * naux < 2^31, a multiple of SW
+  static constexpr int CH_KB = CHUNK_NAUX / SW;     // stages of one exact int32 chunk
   static_assert(2 * ACC_COLS <= 512, "two pass buffers in TMEM");
 };
 
@@ -219,8 +223,9 @@ __device__ __forceinline__ void pe254_issue(uint64_t dA, uint64_t dB, uint32_t d
 }
 
 // MMA issuer over this CTA's stream of stages (units x 2 passes x num_kb),
-// unrolled over the pipeline stages (compile-time shared-memory offsets);
-// pass it uses TMEM buffer it & 1.
+// unrolled over the pipeline stages (compile-time shared-memory offsets). A
+// pass is cut into accumulations of at most CH_KB stages (chunks, nch per
+// pass); accumulation `it` uses TMEM buffer it & 1.
 __device__ __forceinline__ void pe254_mma_role(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
                                                uint64_t* accf_bar, uint64_t* acce_bar,
                                                uint32_t tmem_base, int num_kb, long long total,
@@ -230,9 +235,12 @@ __device__ __forceinline__ void pe254_mma_role(uint8_t* smem, uint64_t* full_bar
   const uint32_t base = smem_u32(smem);
   const uint64_t dA = sdesc_kmajor_noswz(base + C::A_OFF, 128, C::SW * 8);
   const uint64_t dB = sdesc_kmajor_noswz(base + C::B_OFF, 128, C::SW * 8);
+  const int nch = (num_kb + C::CH_KB - 1) / C::CH_KB;
   uint32_t phase = 0;
-  int it = 0;   // passes started
-  int kbp = 0;  // stage within the pass
+  int it = 0;   // accumulations started
+  int kbp = 0;  // stage within the accumulation
+  int ci = 0;   // chunk of the current pass
+  int len = num_kb < C::CH_KB ? num_kb : C::CH_KB;
   uint32_t d_tmem = tmem_base;
   bool stop = false;
   for (long long g = 0; g < total && !stop; g += STAGES) {
@@ -255,10 +263,13 @@ __device__ __forceinline__ void pe254_mma_role(uint8_t* smem, uint64_t* full_bar
       tc_fence_after();
       pe254_issue<S * C::STAGE_BYTES>(dA, dB, d_tmem, kbp == 0);
       tc_commit(&empty_bar[S]);
-      if (++kbp == num_kb) {
+      if (++kbp == len) {
         tc_commit(&accf_bar[it & 1]);
         kbp = 0;
         ++it;
+        ci = (ci + 1 == nch) ? 0 : ci + 1;
+        const int rest = num_kb - ci * C::CH_KB;
+        len = rest < C::CH_KB ? rest : C::CH_KB;
       }
     });
     phase ^= 1u;
@@ -379,39 +390,44 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1) pair_energy254_kernel(const
     const int aloc = 32 * q + lane;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + col0;
     const double c1 = 1.0 / 254.0, c2 = 1.0 / 64516.0, c3 = 1.0 / 16387064.0;
+    const int nch = (num_kb + C::CH_KB - 1) / C::CH_KB;
     double acc = 0.0;
     int it = 0;
     bool aborted = false;
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
       double xt[NCOL], yt[NCOL];
 #pragma unroll
-      for (int pass = 0; pass < 2; ++pass, ++it) {
-        if (!mbar_wait_warp(&accf_bar[pass], (it >> 1) & 1, ab, kTimeoutAccFull)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        uint32_t v0[16], v1[16], v2[16], v3[16];
-        const uint32_t col = lane_base + pass * C::ACC_COLS;
-        tmem_ld16(col, v0);
-        tmem_ld16(col + C::BN, v1);
-        tmem_ld16(col + 2 * C::BN, v2);
-        tmem_ld16(col + 3 * C::BN, v3);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acce_bar[pass]);  // the buffer is free for the pass after next
+      for (int jj = 0; jj < NCOL; ++jj) xt[jj] = yt[jj] = 0.0;
 #pragma unroll
-        for (int jj = 0; jj < NCOL; ++jj) {
-          // smallest diagonal first: S_3 / 254^3 + S_2 / 254^2 + S_1 / 254 + S_0
-          double t = static_cast<double>(static_cast<int>(v3[jj])) * c3;
-          t = fma(static_cast<double>(static_cast<int>(v2[jj])), c2, t);
-          t = fma(static_cast<double>(static_cast<int>(v1[jj])), c1, t);
-          t += static_cast<double>(static_cast<int>(v0[jj]));
-          if (pass == 0)
-            xt[jj] = t;
-          else
-            yt[jj] = t;
+      for (int pass = 0; pass < 2 && !aborted; ++pass) {
+        for (int c = 0; c < nch; ++c, ++it) {
+          const int buf = it & 1;
+          if (!mbar_wait_warp(&accf_bar[buf], (it >> 1) & 1, ab, kTimeoutAccFull)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t col = lane_base + buf * C::ACC_COLS;
+          // one diagonal at a time, smallest first (S_3 / 254^3 + S_2 / 254^2
+          // + S_1 / 254 + S_0), so that only 16 loaded words are live
+#pragma unroll
+          for (int d = C::DMAX; d >= 0; --d) {
+            uint32_t v[16];
+            tmem_ld16(col + d * C::BN, v);
+            tmem_ld_wait();
+            const double cd = d == 3 ? c3 : d == 2 ? c2 : d == 1 ? c1 : 1.0;
+#pragma unroll
+            for (int jj = 0; jj < NCOL; ++jj) {
+              const double sv = static_cast<double>(static_cast<int>(v[jj]));
+              if (pass == 0)
+                xt[jj] = fma(sv, cd, xt[jj]);
+              else
+                yt[jj] = fma(sv, cd, yt[jj]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce_bar[buf]);  // free for the accumulation after next
         }
       }
       if (aborted) break;

@@ -233,12 +233,175 @@ def _panel_gemm(a: torch.Tensor, b_stack: torch.Tensor, pieces: int, C: torch.Te
     N.count_launches(3 if code == N.F32 else 1)
 
 
+# ── operand exchange over NVLink by the copy engines (gemm_2d "p2p") ──────────
+
+_READY = {}      # device index -> (int32 flags tensor, last epoch)
+_COPY_STREAMS = {}  # device index -> copy streams
+_N_COPY_STREAMS = 4
+
+
+def _ready_flags(dev: torch.device, n: int):
+    """This device's readiness flags (at least n) and a fresh epoch."""
+    flags, epoch = _READY.get(dev.index, (None, 0))
+    if flags is None or flags.numel() < n:
+        flags = torch.zeros(max(64, n), dtype=torch.int32, device=dev)
+    epoch = (epoch + 1) & 0x7FFFFFFF or 1
+    _READY[dev.index] = (flags, epoch)
+    return flags, epoch
+
+
+def _copy_streams(dev: torch.device):
+    if dev.index not in _COPY_STREAMS:
+        _COPY_STREAMS[dev.index] = [torch.cuda.Stream(dev) for _ in range(_N_COPY_STREAMS)]
+    return _COPY_STREAMS[dev.index]
+
+
+def _rendezvous(dev: torch.device, group) -> None:
+    """A one-element all-reduce on the current stream: every rank's earlier
+    stream work is done before any rank's later work runs."""
+    t = torch.zeros(1, dtype=torch.int32, device=dev)
+    dist.all_reduce(t, group=group)
+
+
+def _exchange_shards(A_shard: torch.Tensor, B_shard: torch.Tensor, grid: Grid2D):
+    """Every rank's (A shard, B shard) pointers, mapped into this process
+    (CUDA IPC), or None on every rank when any rank cannot export (the
+    decision is collective, so all ranks then take the NCCL path)."""
+    import ctypes
+
+    from . import _native as N
+
+    rec = torch.zeros(2 * 72 + 1, dtype=torch.uint8)
+    ok = True
+    for k, t in enumerate((A_shard, B_shard)):
+        h = (ctypes.c_char * 64)()
+        off = ctypes.c_int64()
+        if N.lib().trnblas_ipc_export(t.data_ptr(), h, ctypes.byref(off)) != 0:
+            ok = False
+            break
+        rec[72 * k : 72 * k + 64] = torch.frombuffer(bytearray(h.raw), dtype=torch.uint8)
+        rec[72 * k + 64 : 72 * k + 72] = torch.frombuffer(bytearray(off.value.to_bytes(8, "little", signed=True)),
+                                                          dtype=torch.uint8)
+    rec[-1] = 1 if ok else 0
+    allrec = torch.empty((grid.world, rec.numel()), dtype=torch.uint8, device=A_shard.device)
+    dist.all_gather_into_tensor(allrec, rec.to(A_shard.device), group=grid.group)
+    allrec = allrec.cpu()
+    if not bool(allrec[:, -1].all()):
+        return None
+    ptrs = []
+    for r in range(grid.world):
+        if r == grid.rank:
+            ptrs.append((A_shard.data_ptr(), B_shard.data_ptr()))
+            continue
+        pair = []
+        for k in range(2):
+            hb = bytes(allrec[r, 72 * k : 72 * k + 64].tolist())
+            off = int.from_bytes(bytes(allrec[r, 72 * k + 64 : 72 * k + 72].tolist()), "little", signed=True)
+            p = ctypes.c_void_p()
+            N.check(N.lib().trnblas_ipc_open(hb, off, ctypes.byref(p)), "trnblas_ipc_open")
+            pair.append(p.value)
+        ptrs.append(tuple(pair))
+    return ptrs
+
+
+def _gemm_2d_p2p(A_shard, B_shard, grid: Grid2D, kernel_events=None):
+    """gemm_2d with the operand exchange overlapped with the GEMM: the shards
+    of this rank's grid row (A) and grid column (B) are copied into local
+    buffers by the copy engines (peer shards pulled over NVLink; no SM, so
+    nothing competes with the GEMM's persistent CTAs), each copy raising a
+    ready flag, while ONE GEMM launch (trnblas_gemm_ready) multiplies: its
+    producer waits for the flags of a tile's A rows and B slab before loading
+    them, and the tile walk starts on this rank's own shards. Returns None
+    (nothing launched) when the shards cannot be shared; the caller then
+    gathers with NCCL."""
+    from . import _native as N
+
+    dev = A_shard.device
+    pr, pc = grid.pr, grid.pc
+    mw, K = A_shard.shape
+    nw = B_shard.shape[1]
+    main = torch.cuda.current_stream(dev)
+    # every rank's shards are written before any peer reads them
+    _rendezvous(dev, grid.group)
+    ptrs = _exchange_shards(A_shard, B_shard, grid)
+    if ptrs is None:
+        return None
+    es = A_shard.element_size()
+    a_full = torch.empty((pc * mw, K), dtype=A_shard.dtype, device=dev)
+    b_full = torch.empty((pr * K, nw), dtype=B_shard.dtype, device=dev)
+    C = torch.empty((pc * mw, pr * nw), dtype=A_shard.dtype, device=dev)
+    flags, epoch = _ready_flags(dev, pc + pr)
+    streams = _copy_streams(dev)
+    for st in streams:
+        st.wait_stream(main)
+    row_ranks = [grid.r * pc + c for c in range(pc)]  # A shard c' of block row r
+    col_ranks = [r * pc + grid.c for r in range(pr)]  # B slab r' of block column c
+    jobs = [("a", grid.c), ("b", grid.r)]
+    jobs += [("b", (grid.r + d) % pr) for d in range(1, pr)]
+    jobs += [("a", (grid.c + d) % pc) for d in range(1, pc)]
+    a_bytes, b_bytes = mw * K * es, K * nw * es
+    for n, (kind, idx) in enumerate(jobs):
+        st = streams[n % len(streams)]
+        if kind == "a":
+            dst, src, nbytes, flag = a_full.data_ptr() + idx * a_bytes, ptrs[row_ranks[idx]][0], a_bytes, idx
+        else:
+            dst, src, nbytes, flag = b_full.data_ptr() + idx * b_bytes, ptrs[col_ranks[idx]][1], b_bytes, pc + idx
+        N.check(N.lib().trnblas_copy_async(dst, src, nbytes, st.cuda_stream), "trnblas_copy_async")
+        N.check(N.lib().trnblas_stream_signal(flags.data_ptr() + 4 * flag, epoch, st.cuda_stream),
+                "trnblas_stream_signal")
+    for t in (a_full, b_full, flags):
+        for st in streams:
+            t.record_stream(st)
+    if kernel_events is not None:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(main)
+    code = N.dtype_code(A_shard.dtype)
+    rc = N.lib().trnblas_gemm_ready(
+        code, pr, pc * mw, nw, K, 1.0,
+        a_full.data_ptr(), K, 0, 0,
+        b_full.data_ptr(), nw, K * nw, 0,
+        0.0, None, 0, 0,
+        C.data_ptr(), pr * nw, nw,
+        flags.data_ptr(), epoch, mw, pc, grid.c * mw, grid.r, main.cuda_stream,
+    )
+    N.check(rc, "trnblas_gemm_ready")
+    N.count_launches(1)
+    if kernel_events is not None:
+        ev1.record(main)
+        kernel_events.append((ev0, ev1))
+    for st in streams:
+        main.wait_stream(st)
+    # every peer has finished pulling from this rank's shards before the
+    # caller may release or overwrite them
+    _rendezvous(dev, grid.group)
+    return C
+
+
+def _p2p_eligible(A_shard, B_shard, grid: Grid2D, k_chunks: int) -> bool:
+    import os
+
+    return (
+        os.environ.get("TRNBLAS_B200_P2P", "1") != "0"
+        and A_shard.device.type == "cuda"
+        and A_shard.dtype in (torch.bfloat16, torch.float16)
+        and B_shard.dtype == A_shard.dtype
+        and grid.world > 1
+        and k_chunks == 1
+        and _local_mm is None
+        and dist.get_backend(grid.group) == "nccl"
+        and A_shard.shape[0] % 256 == 0
+        and A_shard.shape[1] % 8 == 0
+        and B_shard.shape[1] % 8 == 0
+    )
+
+
 def gemm_2d(
     A_shard: torch.Tensor,
     B_shard: torch.Tensor,
     grid: Grid2D,
     k_chunks: int = 1,
     kernel_events: list | None = None,
+    transport: str = "auto",
 ) -> torch.Tensor:
     """This rank's (M/pr) x (N/pc) block of C = A @ B on a pr x pc grid.
 
@@ -255,6 +418,11 @@ def gemm_2d(
     row / column of one rank needs no gather. `kernel_events`, when given,
     receives a (start, end) CUDA event pair around each local GEMM launch on
     the launching stream.
+
+    transport "auto" (default) exchanges the shards of 16-bit operands on
+    GPUs by copy-engine pulls over NVLink overlapped with one GEMM launch
+    (`_gemm_2d_p2p`) and otherwise with NCCL all-gathers; "nccl" forces the
+    latter (TRNBLAS_B200_P2P=0 disables the former).
     """
     pr, pc = grid.pr, grid.pc
     mw, K = A_shard.shape
@@ -271,6 +439,10 @@ def gemm_2d(
     main = torch.cuda.current_stream(dev) if cuda else None
     A_shard = A_shard if A_shard.stride(1) == 1 else A_shard.contiguous()
     B_shard = B_shard.contiguous()
+    if transport == "auto" and K > 0 and _p2p_eligible(A_shard.contiguous(), B_shard, grid, k_chunks):
+        C = _gemm_2d_p2p(A_shard.contiguous(), B_shard, grid, kernel_events)
+        if C is not None:
+            return C
 
     def gather_chunk(k0, k1):
         whole = k0 == 0 and k1 == K

@@ -53,7 +53,10 @@ def _with_workspace(A, B, C, alpha, beta, transA, transB, M, N_, K):
 
 def _two_calls(dev: torch.device):
     g = torch.Generator(device=dev).manual_seed(11)
-    cases = [(300, 200, 517, False, False), (1024, 768, 1536, True, True)]  # 2nd call reuses scratch
+    # odd leading dimensions (517, then 257) send the first two calls through
+    # the split into the built-in scratch, the second on the first's leftover
+    # contents; the third has TMA-aligned operands (split inside the kernel)
+    cases = [(300, 200, 517, False, False), (257, 129, 333, True, False), (1024, 768, 1536, True, True)]
     for M, N_, K, ta, tb in cases:
         A = torch.randn(*((K, M) if ta else (M, K)), device=dev, generator=g)
         B = torch.randn(*((N_, K) if tb else (K, N_)), device=dev, generator=g)

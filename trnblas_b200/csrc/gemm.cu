@@ -221,7 +221,7 @@ int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   }
   const int grid = static_cast<int>(std::min<long long>(p.num_tiles, num_sms()));
   if (p.mode == kModeGemm && use_wave_sync(p.K, p.num_tiles, grid)) p.wave_ctr = wave_counter(stream);
-  kern<<<grid, 192, smem, stream>>>(a0, a1, b0, b1, p);
+  kern<<<grid, Cfg::THREADS, smem, stream>>>(a0, a1, b0, b1, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
   return TRNBLAS_OK;
@@ -469,6 +469,33 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     p.ready_b0 = rs->b0;
     p.rot_b = rs->rot_b;
   }
+  // fp32 with K-major operands the TMA can read (op(A) stored M x K and op(B)
+  // stored N x K, 16-byte aligned bases, row and batch strides multiples of 4
+  // elements): the split fused into the GEMM kernel. (An MN-major tf32
+  // operand needs the 32-byte-atom 128-byte swizzle, which this kernel does
+  // not stage: those operands take the split pass.)
+  auto tma_f32 = [](const void* X, long long ld, long long bstride, bool batched) {
+    return (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ld % 4 == 0 && (!batched || bstride % 4 == 0);
+  };
+  if (dtype == TRNBLAS_F32 && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
+      tma_f32(B, ldb, strideB, b_b)) {
+    const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    p.a_mn = transA ? 1 : 0;
+    p.b_mn = transB ? 0 : 1;
+    p.in_fmt = kFmtTF32;
+    const long long a_rows = transA ? K : M, b_rows = transB ? N : K;
+    const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 4);
+    const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 4);
+    bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 4, A, M, K, nba, lda, sa2, 32, 32)
+                     : encode_map_3d(&ma0, dt, 4, A, K, M, nba, lda, sa2, 32, 128);
+    ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 4, B, N, K, nbb, ldb, sb2, 32, 32)
+                       : encode_map_3d(&mb0, dt, 4, B, K, N, nbb, ldb, sb2, 32, 128));
+    if (!ok) return TRNBLAS_ERR_ALIGN;
+    p.tiles_m = static_cast<int>(ceil_div(M, 128));
+    p.tiles_n = static_cast<int>(ceil_div(N, 128));
+    p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+    return launch_gemm<kTF32x3F, 128, 3>(ma0, ma0, mb0, mb0, p, stream);
+  }
   if (dtype == TRNBLAS_F32) {
     const size_t need = trnblas_gemm_workspace_size(dtype, batch, M, N, K, strideA, strideB);
     if (!workspace || workspace_bytes < need) {
@@ -626,6 +653,17 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
     return TRNBLAS_ERR_ARG;
   }
   CUtensorMap ma0, ma1;
+  if (dtype == TRNBLAS_F32 && !trans && (reinterpret_cast<uintptr_t>(A) & 15) == 0 && lda % 4 == 0) {
+    // the split fused into the kernel: raw fp32 tiles of A for both operands
+    const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    p.a_mn = p.b_mn = trans ? 1 : 0;
+    p.in_fmt = kFmtTF32;
+    const long long s2 = round_up(lda * (trans ? k : n), 4);
+    const bool ok = trans ? encode_map_3d(&ma0, dt, 4, A, n, k, 1, lda, s2, 32, 32)
+                          : encode_map_3d(&ma0, dt, 4, A, k, n, 1, lda, s2, 32, 128);
+    if (!ok) return TRNBLAS_ERR_ALIGN;
+    return launch_gemm<kTF32x3F, 128, 3>(ma0, ma0, ma0, ma0, p, stream);
+  }
   if (dtype == TRNBLAS_F32) {
     const size_t need = trnblas_syrk_workspace_size(dtype, n, k);
     if (!workspace || workspace_bytes < need) {

@@ -29,7 +29,14 @@
 
 namespace tb {
 
-enum GemmKind : int { kF16 = 0, kTF32x3 = 1 };
+// kTF32x3F: the fp32 API with the split fused into the kernel: TMA loads the
+// raw fp32 tiles (K- or MN-major) into the "hi" slots and converter warps
+// write lo = x - trunc19(x) beside them. The tensor core reads only the top
+// 19 bits of a kind::tf32 operand (measured: a product of raw fp32 inputs
+// equals the product of inputs truncated to tf32 within the fp32 accumulate
+// rounding, 6e-8, and differs from rounded inputs by 1.2e-3), so the raw tile
+// serves as hi and hi + lo = x exactly; no hi / lo planes in global memory.
+enum GemmKind : int { kF16 = 0, kTF32x3 = 1, kTF32x3F = 2 };
 enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
 // kModeSyrk: lower-triangle BM x BM tiles; kModeSyrkWide: BM x BN tiles
 // (BN = 2 BM) over the lower triangle's column-block pairs, row m holding
@@ -110,6 +117,14 @@ __device__ __forceinline__ void soft_wave_wait(const int* ctr, int target,
   }
 }
 
+// x - trunc19(x): the part of x below the 19 bits a kind::tf32 operand keeps
+// (exact in fp32); 0 for inf / nan.
+__device__ __forceinline__ float tf32_lo(float x) {
+  const uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) == 0x7F800000u) return 0.0f;
+  return x - __uint_as_float(u & 0xFFFFE000u);
+}
+
 // Shared memory after the pipeline stages: 256 bytes of barriers, then one
 // 4 KB transpose stage per epilogue warp (SYRK mirror stores).
 constexpr int kGemmBarBytes = 256;
@@ -118,23 +133,29 @@ constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;
 template <int KIND, int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
+  static constexpr bool TF32 = (KIND == kTF32x3 || KIND == kTF32x3F);
   static constexpr int ESIZE = (KIND == kF16) ? 2 : 4;
   static constexpr int BK = 128 / ESIZE;  // one 128-byte swizzle row of K
-  static constexpr int NPARTS = (KIND == kTF32x3) ? 2 : 1;  // hi/lo
+  static constexpr int NPARTS = TF32 ? 2 : 1;  // hi/lo
   static constexpr int A_TILE = BM * 128;  // bytes of one A part
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE_BYTES = NPARTS * (A_TILE + B_TILE);
+  // bytes the TMA loads per stage (the fused split computes the lo parts)
+  static constexpr int LOAD_BYTES = (KIND == kTF32x3F) ? (A_TILE + B_TILE) : STAGE_BYTES;
+  // warps: producer, MMA, 4 epilogue, and 2 converters for the fused split
+  static constexpr int CONV_WARPS = 2;
+  static constexpr int THREADS = 32 * (6 + ((KIND == kTF32x3F) ? CONV_WARPS : 0));
   // K blocks accumulated in TMEM before the epilogue takes the partial sum.
   // The tensor core accumulates fp32 with truncation, whose bias grows with
   // the number of accumulations; for the fp32 API the partial sums of 128-wide
   // K chunks are added in the epilogue with round-to-nearest instead, which
   // bounds the relative error near 1e-6 at any K. bf16 / fp16 results round
   // their output far above that bias, so they accumulate the whole K in TMEM.
-  static constexpr int CHUNK_KB = (KIND == kTF32x3) ? 4 : (1 << 30);
-  static constexpr int NBUF = (KIND == kTF32x3) ? 4 : 2;  // TMEM accumulator buffers
+  static constexpr int CHUNK_KB = TF32 ? 4 : (1 << 30);
+  static constexpr int NBUF = TF32 ? 4 : 2;  // TMEM accumulator buffers
   static constexpr int TMEM_COLS = (NBUF * BN <= 32) ? 32 : (NBUF * BN <= 64) ? 64 : (NBUF * BN <= 128) ? 128 : (NBUF * BN <= 256) ? 256 : 512;
   static_assert(NBUF * BN <= 512, "TMEM holds 512 columns");
-  static_assert(KIND != kTF32x3 || BN == 128, "chunked epilogue keeps 128 columns in registers");
+  static_assert(!TF32 || BN == 128, "chunked epilogue keeps 128 columns in registers");
 };
 
 // MMA issuer role over this CTA's stream of K blocks (tiles x num_kb), chunked
@@ -151,6 +172,8 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
                                               uint64_t* full_bar, uint64_t* empty_bar,
                                               uint64_t* accf_bar, uint64_t* acce_bar,
                                               uint32_t tmem_base, int num_kb, const Abort& ab) {
+  // full_bar: the stage's operands are complete (for kTF32x3F the converters'
+  // barriers, which follow the TMA loads and the lo parts)
   using Cfg = GemmCfg<KIND, BN>;
   constexpr int SB = Cfg::STAGE_BYTES;
   const uint32_t idesc_v = idesc(kAccF32, p.in_fmt, p.in_fmt, p.a_mn, p.b_mn, Cfg::BM, BN);
@@ -161,10 +184,18 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
   uint64_t ad[4], bd[4];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
-    ad[kk] = (KIND == kF16 && p.a_mn) ? sdesc_sw128(sa0 + kk * 2048, 64 * 128, 1024)
-                                      : sdesc_sw128(sa0 + kk * 32, 16, 1024);
-    bd[kk] = (KIND == kF16 && p.b_mn) ? sdesc_sw128(sb0 + kk * 2048, 64 * 128, 1024)
-                                      : sdesc_sw128(sb0 + kk * 32, 16, 1024);
+    // MN-major: boxes of one 128-byte swizzle row of MN x BK K-rows, LBO the
+    // box bytes, one k step = K rows of the MMA (16 for 16-bit, 8 for tf32)
+    if constexpr (KIND == kF16) {
+      ad[kk] = p.a_mn ? sdesc_sw128(sa0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sa0 + kk * 32, 16, 1024);
+      bd[kk] = p.b_mn ? sdesc_sw128(sb0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sb0 + kk * 32, 16, 1024);
+    } else if constexpr (KIND == kTF32x3F) {
+      ad[kk] = p.a_mn ? sdesc_sw128(sa0 + kk * 1024, 32 * 128, 1024) : sdesc_sw128(sa0 + kk * 32, 16, 1024);
+      bd[kk] = p.b_mn ? sdesc_sw128(sb0 + kk * 1024, 32 * 128, 1024) : sdesc_sw128(sb0 + kk * 32, 16, 1024);
+    } else {
+      ad[kk] = sdesc_sw128(sa0 + kk * 32, 16, 1024);
+      bd[kk] = sdesc_sw128(sb0 + kk * 32, 16, 1024);
+    }
   }
   const int my_tiles =
       p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -437,7 +468,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int 
 }
 
 template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<KIND, BN>::THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a0,
                       const __grid_constant__ CUtensorMap map_a1,
                       const __grid_constant__ CUtensorMap map_b0,
@@ -450,13 +481,14 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  static_assert((2 * STAGES + 2 * Cfg::NBUF + 1) * 8 + 8 <= kGemmBarBytes, "barrier block");
+  static_assert((3 * STAGES + 2 * Cfg::NBUF + 1) * 8 + 8 <= kGemmBarBytes, "barrier block");
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;   // [NBUF]
   uint64_t* acce_bar = accf_bar + Cfg::NBUF;  // [NBUF]
   uint64_t* drain_bar = acce_bar + Cfg::NBUF; // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* conv_bar = drain_bar + 1;         // [STAGES] kTF32x3F: lo parts written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv_bar + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -467,6 +499,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], Cfg::CONV_WARPS);
     }
     for (int a = 0; a < Cfg::NBUF; ++a) {
       mbar_init(&accf_bar[a], 1);
@@ -518,9 +551,25 @@ __global__ void __launch_bounds__(192, 1)
         }
         uint8_t* sa = smem + stage * STAGE_BYTES;
         uint8_t* sb = sa + Cfg::NPARTS * Cfg::A_TILE;
-        mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::LOAD_BYTES);
         const int k0 = kb * BK;
-        if (KIND == kF16) {
+        if (KIND == kTF32x3F) {
+          // raw fp32 tiles into the hi slots (MN-major: boxes of 32 MN x 32 K)
+          if (!p.a_mn) {
+            tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tma_load_3d(sa + j * (32 * 128), &map_a0, &full_bar[stage], m0 + 32 * j, k0, za);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sb, &map_b0, &full_bar[stage], k0, n0, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_3d(sb + j * (32 * 128), &map_b0, &full_bar[stage], n0 + 32 * j, k0, zb);
+          }
+        } else if (KIND == kF16) {
           if (!p.a_mn) {
             tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
           } else {
@@ -568,8 +617,8 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    gemm_mma_role<KIND, BN, STAGES>(p, smem, full_bar, empty_bar, accf_bar, acce_bar, tmem_base,
-                                    num_kb, ab);
+    gemm_mma_role<KIND, BN, STAGES>(p, smem, KIND == kTF32x3F ? conv_bar : full_bar, empty_bar,
+                                    accf_bar, acce_bar, tmem_base, num_kb, ab);
     // Every MMA this thread issued must finish before TMEM is released.
     tc_commit(drain_bar);
     const unsigned long long t0 = globaltimer_ns();
@@ -579,7 +628,46 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
     }
-  } else if (warp >= 2) {
+  } else if (KIND == kTF32x3F && warp >= 6) {
+    // ------------------------------------------------------------ converters
+    // For every stage, in the producer's order: lo = x - trunc19(x) of the
+    // raw A and B tiles, written beside them (same swizzled offsets; the
+    // split is elementwise). inf / nan keep lo = 0.
+    constexpr int CT = 32 * Cfg::CONV_WARPS;
+    const int ct = threadIdx.x - 192;  // 0 .. CT - 1
+    const int my_tiles =
+        p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const long long total = static_cast<long long>(my_tiles) * num_kb;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long g = 0; g < total; ++g) {
+      if (!mbar_wait_warp(&full_bar[stage], phase, ab, kTimeoutAux)) break;
+      uint8_t* st = smem + stage * STAGE_BYTES;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int bytes = part == 0 ? Cfg::A_TILE : Cfg::B_TILE;
+        const float4* hi = reinterpret_cast<const float4*>(st + (part == 0 ? 0 : 2 * Cfg::A_TILE));
+        float4* lo = reinterpret_cast<float4*>(st + (part == 0 ? Cfg::A_TILE : 2 * Cfg::A_TILE + Cfg::B_TILE));
+#pragma unroll 4
+        for (int i = ct; i < bytes / 16; i += CT) {
+          const float4 x = hi[i];
+          float4 l;
+          l.x = tf32_lo(x.x);
+          l.y = tf32_lo(x.y);
+          l.z = tf32_lo(x.z);
+          l.w = tf32_lo(x.w);
+          lo[i] = l;
+        }
+      }
+      fence_proxy_async_smem();  // the MMA (async proxy) reads what these stores wrote
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv_bar[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  } else if (warp >= 2 && warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = 32 * q + lane;

@@ -100,6 +100,20 @@ TRNBLAS_API int trnblas_gemm_f32_noalloc(int64_t M, int64_t N, int64_t K, float 
                              void* stream);
 
 /*
+ * trnblas_gemm with one triangular operand (trmm): tri = 1 / 2 when op(A) is
+ * lower / upper triangular, 3 / 4 when op(B) is, holding exact zeros outside
+ * the triangle. Each output tile multiplies only the K blocks its rows (A) or
+ * columns (B) reach, about half the products of the dense GEMM; tri = 0 is
+ * trnblas_gemm. Replaces the triangular multiply of the reference's trmm
+ * (trnblas/level3.py:383-417), which multiplies the masked triangle densely.
+ */
+TRNBLAS_API int trnblas_gemm_tri(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                     const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                     int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                     int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD, int tri,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * bf16 / fp16 trnblas_gemm (no workspace) whose operands arrive while it runs:
  * rows [s * shard_rows, (s + 1) * shard_rows) of op(A) may be read once
  * ready[s] has reached `epoch` (wrap-safe), batch entry b of op(B) once

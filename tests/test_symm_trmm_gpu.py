@@ -63,3 +63,24 @@ def test_symm_trmm_bf16_and_large():
         T = tb.trmm(2.0, A.to(dt), B.to(dt), uplo="upper", trans=True)
         ref = blas3.trmm(2.0, A.to(dt).float().cpu().numpy(), B.to(dt).float().cpu().numpy(), "left", "upper", True)
         assert T.dtype == dt and blas3.relf(T.float().cpu().numpy(), ref) <= tol
+
+
+@pytest.mark.parametrize("dt,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
+def test_trmm_triangle_blocks_every_case(dt, tol):
+    """The GEMM kernel skips the K blocks outside the triangle (triangular
+    op(A) on the left, triangular op(B) on the right, lower or upper): every
+    case at a ragged size spanning many K blocks against the fp64 product of
+    the masked triangle."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    n, m = 1300, 520
+    A = torch.randn(n, n, device="cuda", generator=g).to(dt)
+    for side in ("left", "right"):
+        X = torch.randn(*((n, m) if side == "left" else (m, n)), device="cuda", generator=g).to(dt)
+        for uplo in ("lower", "upper"):
+            for trans in (False, True):
+                R = tb.trmm(0.5, A, X, side=side, uplo=uplo, trans=trans)
+                T = torch.tril(A.double()) if uplo == "lower" else torch.triu(A.double())
+                T = T.T if trans else T
+                ref = 0.5 * (T @ X.double() if side == "left" else X.double() @ T)
+                assert R.dtype == dt
+                assert blas3.relf(R.double().cpu().numpy(), ref.cpu().numpy()) <= tol, (side, uplo, trans)

@@ -37,6 +37,11 @@ _SIGNATURES = {
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
          _i64, _p, _i64, _i64, _p, _sz, _p],
     ),
+    "trnblas_gemm_tri": (
+        _i,
+        [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
+         _i64, _p, _i64, _i64, _i, _p, _sz, _p],
+    ),
     "trnblas_gemm_ready": (
         _i,
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,

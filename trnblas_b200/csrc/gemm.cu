@@ -388,7 +388,8 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
                      const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
                      int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
                      int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
-                     void* workspace, size_t workspace_bytes, void* stream_, const ReadySpec* rs) {
+                     void* workspace, size_t workspace_bytes, void* stream_, const ReadySpec* rs,
+                     int tri = 0) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (int rc = check_dims(batch, M, N, K)) return rc;
   if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
@@ -447,6 +448,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   // bands of 12 row tiles: with the wave synchronisation, the lowest energy
   // per flop measured at 32768^3 under the power cap (widths 4 .. 16 swept)
   p.group_m = group_m_override() ? group_m_override() : 12;
+  p.tri = tri;
   p.status = status;
   p.timeout_ns = wait_timeout_ns();
   const bool a_b = strideA != 0 && batch > 1;
@@ -582,6 +584,20 @@ int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, floa
   return gemm_impl(dtype, batch, M, N, K, alpha, A, lda, strideA, transA, B, ldb, strideB, transB,
                    beta, C, ldc, strideC, D, ldd, strideD, workspace, workspace_bytes, stream,
                    nullptr);
+}
+
+int trnblas_gemm_tri(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+                     const void* A, int64_t lda, int64_t strideA, int transA, const void* B,
+                     int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
+                     int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD, int tri,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (tri < 0 || tri > 4) {
+    set_error("trnblas_gemm_tri: tri must be 0 .. 4");
+    return TRNBLAS_ERR_ARG;
+  }
+  return gemm_impl(dtype, batch, M, N, K, alpha, A, lda, strideA, transA, B, ldb, strideB, transB,
+                   beta, C, ldc, strideC, D, ldd, strideD, workspace, workspace_bytes, stream,
+                   nullptr, tri);
 }
 
 int trnblas_gemm_ready(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,

@@ -75,7 +75,27 @@ struct GemmParams {
   int ready_epoch;
   int shard_tiles_m, ready_b0;
   int rot_m, rot_b;
+  // Triangular operand (trmm): 0 none; op(A) 1 lower / 2 upper; op(B)
+  // 3 lower / 4 upper. The operand holds exact zeros outside its triangle,
+  // and each tile runs only the K blocks its rows (A) or columns (B) reach.
+  int tri;
 };
+
+// K blocks [lo, hi) a tile with rows [m0, m0 + bm) and columns [n0, n0 + bn)
+// runs (all of them unless an operand is triangular; at least one block).
+__device__ __forceinline__ void tile_k_range(const GemmParams& p, int m0, int bm, int n0, int bn,
+                                             int bk, int num_kb, int& lo, int& hi) {
+  lo = 0;
+  hi = num_kb;
+  if (p.tri == 1) hi = min(num_kb, (m0 + bm + bk - 1) / bk);  // A[m][k] = 0 for k > m
+  if (p.tri == 2) lo = min(num_kb, m0 / bk);                    // A[m][k] = 0 for k < m
+  if (p.tri == 3) lo = min(num_kb, n0 / bk);                    // B[k][n] = 0 for k < n
+  if (p.tri == 4) hi = min(num_kb, (n0 + bn + bk - 1) / bk);  // B[k][n] = 0 for k > n
+  if (hi <= lo) {
+    lo = min(lo, num_kb - 1);
+    hi = lo + 1;
+  }
+}
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
@@ -167,6 +187,8 @@ struct GemmCfg {
 // it, and scalar work between the MMAs of consecutive stages (stage index
 // arithmetic, layout selects, descriptor rebuilds) shows up as idle tensor
 // cycles.
+__device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz, int& mb, int& nb);
+
 template <int KIND, int BN, int STAGES>
 __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem,
                                               uint64_t* full_bar, uint64_t* empty_bar,
@@ -199,7 +221,22 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
   }
   const int my_tiles =
       p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const long long total = static_cast<long long>(my_tiles) * num_kb;
+  // K blocks of this CTA's ti-th tile (fewer than num_kb only for a
+  // triangular operand)
+  auto tile_kb = [&](int ti) -> int {
+    if (!p.tri) return num_kb;
+    int bz, mb, nb, lo, hi;
+    decode_tile(p, static_cast<int>(blockIdx.x) + ti * static_cast<int>(gridDim.x), bz, mb, nb);
+    tile_k_range(p, mb * Cfg::BM, Cfg::BM, nb * BN, BN, Cfg::BK, num_kb, lo, hi);
+    return hi - lo;
+  };
+  long long total = static_cast<long long>(my_tiles) * num_kb;
+  if (p.tri) {
+    total = 0;
+    for (int ti = 0; ti < my_tiles; ++ti) total += tile_kb(ti);
+  }
+  int ti = 0;
+  int cnt = my_tiles > 0 ? tile_kb(0) : 0;  // K blocks of the current tile
   uint32_t phase = 0;
   int gc = 0;   // accumulation chunks started
   int kbt = 0;  // K block within the tile
@@ -243,11 +280,15 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
       tc_commit(&empty_bar[S]);
       ++kbt;
       ++kbc;
-      if (kbc == Cfg::CHUNK_KB || kbt == num_kb) {
+      if (kbc == Cfg::CHUNK_KB || kbt == cnt) {
         tc_commit(&accf_bar[gc % Cfg::NBUF]);
         ++gc;
         kbc = 0;
-        if (kbt == num_kb) kbt = 0;
+        if (kbt == cnt) {
+          kbt = 0;
+          ++ti;
+          cnt = ti < my_tiles ? tile_kb(ti) : 0;
+        }
       }
     });
     phase ^= 1u;
@@ -544,7 +585,9 @@ __global__ void __launch_bounds__(GemmCfg<KIND, BN>::THREADS, 1)
       const int n0 = nb * ((p.mode == kModeSyrk) ? BM : BN);
       const int za = p.a_batched ? bz : 0;
       const int zb = p.b_batched ? bz : 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
+      int kb_lo, kb_hi;
+      tile_k_range(p, m0, BM, n0, BN, BK, num_kb, kb_lo, kb_hi);
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
           aborted = true;
           break;
@@ -712,7 +755,9 @@ __global__ void __launch_bounds__(GemmCfg<KIND, BN>::THREADS, 1)
         float sum[BN];
 #pragma unroll
         for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
-        for (int kb0 = 0; kb0 < num_kb; kb0 += Cfg::CHUNK_KB, ++gc) {
+        int kb_lo, kb_hi;
+        tile_k_range(p, mb * BM, BM, n0, BN, BK, num_kb, kb_lo, kb_hi);
+        for (int kb0 = kb_lo; kb0 < kb_hi; kb0 += Cfg::CHUNK_KB, ++gc) {
           const int buf = gc % Cfg::NBUF;
           const uint32_t bph = (gc / Cfg::NBUF) & 1;
           if (!mbar_wait_warp(&accf_bar[buf], bph, ab, kTimeoutAccFull)) {

@@ -63,6 +63,16 @@ __device__ __forceinline__ void gemm_pair_mma_role(const GemmParams& p, uint8_t*
     ad[kk] = p.a_mn ? sdesc_sw128(sa0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sa0 + kk * 32, 16, 1024);
     bd[kk] = p.b_mn ? sdesc_sw128(sb0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sb0 + kk * 32, 16, 1024);
   }
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  auto tile_kb = [&](int ti) -> int {  // K blocks of the pair's ti-th tile
+    if (!p.tri) return num_kb;
+    int bz, mb, nb, lo, hi;
+    decode_tile(p, pair + ti * npairs, bz, mb, nb);
+    tile_k_range(p, mb * Cfg::BM, Cfg::BM, nb * Cfg::BN, Cfg::BN, Cfg::BK, num_kb, lo, hi);
+    return hi - lo;
+  };
+  int ti = 0;
+  int cnt = total > 0 ? tile_kb(0) : 0;
   uint32_t phase = 0;
   int gc = 0;
   int kbt = 0;
@@ -93,10 +103,11 @@ __device__ __forceinline__ void gemm_pair_mma_role(const GemmParams& p, uint8_t*
         mma_f16_pair(d_tmem, sdesc_add(ad[kk], OFF), sdesc_add(bd[kk], OFF), idesc_v,
                      (kbt == 0 && kk == 0) ? 0u : 1u);
       tc_commit_pair(&empty_bar[S], 0x3);
-      if (++kbt == num_kb) {
+      if (++kbt == cnt) {
         tc_commit_pair(&accf_bar[gc & 1], 0x3);
         ++gc;
         kbt = 0;
+        cnt = tile_kb(++ti);
       }
     });
     phase ^= 1u;
@@ -153,6 +164,16 @@ __global__ void __launch_bounds__(192, 1)
 
   const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
   const int my_tiles = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
+  long long my_total = static_cast<long long>(my_tiles) * num_kb;  // K blocks of the pair's walk
+  if (p.tri) {
+    my_total = 0;
+    for (int t = pair; t < p.num_tiles; t += npairs) {
+      int bz, mb, nb, lo, hi;
+      decode_tile(p, t, bz, mb, nb);
+      tile_k_range(p, mb * Cfg::BM, Cfg::BM, nb * Cfg::BN, Cfg::BN, Cfg::BK, num_kb, lo, hi);
+      my_total += hi - lo;
+    }
+  }
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -175,7 +196,9 @@ __global__ void __launch_bounds__(192, 1)
       const int n0 = nb * Cfg::BN + Cfg::HN * static_cast<int>(rank);
       const int za = p.a_batched ? bz : 0;
       const int zb = p.b_batched ? bz : 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
+      int kb_lo, kb_hi;
+      tile_k_range(p, mb * Cfg::BM, Cfg::BM, nb * Cfg::BN, Cfg::BN, Cfg::BK, num_kb, kb_lo, kb_hi);
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
           aborted = true;
           break;
@@ -228,7 +251,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ------------------------------------------------------------ MMA issuer (leader)
     gemm_pair_mma_role<STAGES>(p, smem, full_bar, empty_bar, accf_bar, acce_bar, tmem_base, num_kb,
-                               static_cast<long long>(my_tiles) * num_kb, ab);
+                               my_total, ab);
     tc_commit_pair(drain_bar, 0x1);
     const unsigned long long t0 = globaltimer_ns();
     while (!mbar_try_wait(drain_bar, 0)) {

@@ -88,8 +88,10 @@ def _tma_operand(x: torch.Tensor, esize: int):
     return buf, ld, False
 
 
-def _gemm2d(a: torch.Tensor, b: torch.Tensor, alpha: float, beta: float, C) -> torch.Tensor:
-    """alpha * a @ b (+ beta * C when C is a same-shape, same-dtype matrix) on the kernel."""
+def _gemm2d(a: torch.Tensor, b: torch.Tensor, alpha: float, beta: float, C, tri: int = 0) -> torch.Tensor:
+    """alpha * a @ b (+ beta * C when C is a same-shape, same-dtype matrix) on the kernel.
+    tri: 1 / 2 when a is lower / upper triangular, 3 / 4 when b is (exact zeros
+    outside the triangle): the all-zero K blocks are skipped."""
     M, K = a.shape
     K2, Nn = b.shape
     if K != K2:
@@ -114,14 +116,15 @@ def _gemm2d(a: torch.Tensor, b: torch.Tensor, alpha: float, beta: float, C) -> t
         ldc = c_arg.stride(0)
     ws_bytes = N.lib().trnblas_gemm_workspace_size(code, 1, M, Nn, K, 0, 0)
     ws = N.workspace(ws_bytes, dev)
-    rc = N.lib().trnblas_gemm(
-        code, 1, M, Nn, K, float(alpha),
-        N.ptr(at), lda, 0, int(ta),
-        N.ptr(bt), ldb, 0, int(tb),
-        float(beta) if c_arg is not None else 0.0, N.ptr(c_arg), ldc, 0,
-        N.ptr(out), Nn, 0,
-        N.ptr(ws), ws_bytes, N.stream_ptr(dev),
-    )
+    args = (code, 1, M, Nn, K, float(alpha),
+            N.ptr(at), lda, 0, int(ta),
+            N.ptr(bt), ldb, 0, int(tb),
+            float(beta) if c_arg is not None else 0.0, N.ptr(c_arg), ldc, 0,
+            N.ptr(out), Nn, 0)
+    if tri:
+        rc = N.lib().trnblas_gemm_tri(*args, int(tri), N.ptr(ws), ws_bytes, N.stream_ptr(dev))
+    else:
+        rc = N.lib().trnblas_gemm(*args, N.ptr(ws), ws_bytes, N.stream_ptr(dev))
     N.check(rc, "trnblas_gemm")
     N.count_launches(3 if code == N.F32 and K > 0 else 1)  # (2 split kernels +) GEMM
     return out
@@ -785,7 +788,9 @@ def trmm(
     alpha * op(tri(A)) @ B (side 'left') or alpha * B @ op(tri(A)) ('right'),
     tri(A) the `uplo` triangle of A (diagonal ones for diag 'unit'). The
     triangle is masked on the operands' device and multiplied on the GEMM
-    kernel; op = transpose is read in place (no transposed copy)."""
+    kernel, which skips the K blocks that lie wholly outside the triangle
+    (about half the products of a dense GEMM); op = transpose is read in
+    place (no transposed copy)."""
     side, uplo, diag = side_flag(side), uplo_flag(uplo), diag_flag(diag)
     trans = trans_flag(trans)
     if A.dim() != 2 or A.shape[0] != A.shape[1]:
@@ -798,5 +803,16 @@ def trmm(
         tri.diagonal().fill_(1)
     mat = tri.mT if trans else tri
     b = _to(B, dev)
+    if dev.type == "cuda" and a.dtype in N.KERNEL_DTYPES and b.dtype == a.dtype and b.dim() == 2:
+        lower = (uplo == "lower") != trans  # op(tri(A)) is lower triangular
+        if side == "left":
+            if b.shape[0] != mat.shape[1]:
+                raise ValueError(f"trmm: A is {tuple(A.shape)} but B is {tuple(B.shape)} for side='left'")
+            r = _gemm2d(mat, b, alpha, 0.0, None, tri=1 if lower else 2)
+        else:
+            if b.shape[1] != mat.shape[0]:
+                raise ValueError(f"trmm: A is {tuple(A.shape)} but B is {tuple(B.shape)} for side='right'")
+            r = _gemm2d(b, mat, alpha, 0.0, None, tri=3 if lower else 4)
+        return _home(r, home, dev)
     r = gemm(alpha, mat, b) if side == "left" else gemm(alpha, b, mat)
     return _home(r, home, dev)

@@ -250,13 +250,16 @@ FLUSHED = ("syrk", "syrk_bf16", "batched_bf16", "gemm1024")
 # summaries with their commands are under profiles/, named in the comments).
 # None where no capture of the timed shape exists.
 TRAFFIC = {
-    "gemm8192_bf16": 1136268400,   # profiles/gemm_bf16_8192.md
+    "spmd_bf16_1x1": 70950000000,  # profiles/gemm_bf16_32768.md
+    "gemm8192_bf16": 1199138448,   # profiles/gemm_bf16_8192.md
     "gemm8192_fp32": 6728923480,   # profiles/gemm_fp32_8192.md
     "batched": 313154560,          # profiles/gemm_batched_64x512.md
     "batched_bf16": 70896640,      # profiles/gemm_batched_bf16.md
     "syrk": 528911104,             # profiles/gemm_syrk_4096.md
     "syrk_bf16": 34854912,         # profiles/gemm_syrk_bf16_4096.md
     "gemm_fp64": 2161969960,       # profiles/ozaki_fp64_4096.md (the int8 GEMM kernel)
+    "pair3": 1991894560,           # profiles/pair_energy_pair3.md
+    "pair5x4": 4592494720,         # profiles/pair_energy_pair5x4.md
 }
 
 
@@ -758,7 +761,7 @@ def run_dfmp2(args, rank, world, gpu):
         "tflops_fp32_equiv": round(flops / (ms / 1e3) / 1e12, 2),
         "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": 2.0 * pk["bf16_tflops"],
                      "unit": "TOP/s (int8)", "frac": round(ach / (2.0 * pk["bf16_tflops"]), 4),
-                     "kernel": "pair_energy_kernel (energy stage)", "stage_ms": round(e_ms, 3),
+                     "kernel": "pair_energy254_kernel (energy stage)", "stage_ms": round(e_ms, 3),
                      "traffic": None, "peak_source": f"{src}: 2 x bf16 burst (int8 dense rate)"},
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d * world),
                 "d2h_bytes_per_step": 8 * world, "path": "parallel.df_mp2_energy on host inputs"},

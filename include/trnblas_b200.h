@@ -84,9 +84,8 @@ TRNBLAS_API int trnblas_gemm(int dtype, int64_t batch, int64_t M, int64_t N, int
  * beta * C with the argument meanings of trnblas_gemm, for callers that may
  * not allocate device memory when they multiply (plugins whose host owns all
  * device memory, loops where cudaMalloc's device synchronisation is not
- * allowed). Its split scratch (used when an operand's layout keeps the
- * 3xTF32 split out of the kernel: an unaligned base or a row stride that is
- * not a multiple of 4) is a 64 MiB array built into the library and held on
+ * allowed). Its scratch for the 3xTF32 split planes (written by the split
+ * pass before the GEMM kernel) is a 64 MiB array built into the library and held on
  * every GPU that loads it; problems with 2 * (M + N) * round_up(K, 4) * 4
  * bytes of split planes above that are rejected (TRNBLAS_ERR_WORKSPACE).
  * The first call on a device looks up the array's address (make it before any

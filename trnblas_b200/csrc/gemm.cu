@@ -286,6 +286,21 @@ bool use_pair_gemm(long long M, long long N) {
   return mode != 0 && M > 128 && N > 128;
 }
 
+// fp32 (3xTF32) with the split fused into the GEMM kernel (kTF32x3F) instead
+// of the split pass. Off unless TRNBLAS_B200_TF32_FUSED=1: the 3xTF32 MMAs of
+// 128 x 128 tiles already take about all of the SM's shared-memory read
+// bandwidth (8 KB a 64-cycle K step), and the converter warps' reads and
+// writes of every stage come on top, where the split pass adds only the TMA
+// writes of the lo tiles. Measured at 8192^3: fused 115 TFLOP/s against
+// 207 TFLOP/s for the split pass plus GEMM.
+bool use_fused_tf32() {
+  static const int mode = [] {
+    const char* s = std::getenv("TRNBLAS_B200_TF32_FUSED");
+    return (s && *s) ? std::atoi(s) : 0;
+  }();
+  return mode != 0;
+}
+
 // Bytes of one fp32 split plane (R x Kp) for `nb` batch entries, 256-aligned.
 size_t plane_bytes(long long nb, long long R, long long K) {
   const long long kp = round_up(std::max<long long>(K, 1), 4);
@@ -473,13 +488,13 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   }
   // fp32 with K-major operands the TMA can read (op(A) stored M x K and op(B)
   // stored N x K, 16-byte aligned bases, row and batch strides multiples of 4
-  // elements): the split fused into the GEMM kernel. (An MN-major tf32
-  // operand needs the 32-byte-atom 128-byte swizzle, which this kernel does
-  // not stage: those operands take the split pass.)
+  // elements), when use_fused_tf32(): the split fused into the GEMM kernel.
+  // (An MN-major tf32 operand needs the 32-byte-atom 128-byte swizzle, which
+  // this kernel does not stage: those operands take the split pass.)
   auto tma_f32 = [](const void* X, long long ld, long long bstride, bool batched) {
     return (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ld % 4 == 0 && (!batched || bstride % 4 == 0);
   };
-  if (dtype == TRNBLAS_F32 && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
+  if (dtype == TRNBLAS_F32 && use_fused_tf32() && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
       tma_f32(B, ldb, strideB, b_b)) {
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     p.a_mn = transA ? 1 : 0;
@@ -669,7 +684,8 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
     return TRNBLAS_ERR_ARG;
   }
   CUtensorMap ma0, ma1;
-  if (dtype == TRNBLAS_F32 && !trans && (reinterpret_cast<uintptr_t>(A) & 15) == 0 && lda % 4 == 0) {
+  if (dtype == TRNBLAS_F32 && use_fused_tf32() && !trans && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+      lda % 4 == 0) {
     // the split fused into the kernel: raw fp32 tiles of A for both operands
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     p.a_mn = p.b_mn = trans ? 1 : 0;

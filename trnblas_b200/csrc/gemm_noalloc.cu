@@ -5,12 +5,11 @@
 // owns every device allocation, or a latency-critical loop in which
 // cudaMalloc (which can synchronise the device and stall other streams) is
 // not allowed. trnblas_gemm's fp32 path needs scratch for its 3xTF32 operand
-// split whenever an operand's layout keeps the split out of the GEMM kernel
-// (a base that is not 16-byte aligned or a row stride that is not a multiple
-// of 4 elements: then a separate pass writes hi / lo planes); this variant
-// takes that scratch from a fixed array compiled into the library instead of
-// from the caller. (Operands the TMA can read are split inside the kernel and
-// leave the array untouched.)
+// split (a pass that writes hi / lo planes before the GEMM kernel reads
+// them; only K-major operands the TMA can read, with the split fused into the
+// kernel by TRNBLAS_B200_TF32_FUSED=1, go without); this variant takes that
+// scratch from a fixed array compiled into the library instead of from the
+// caller.
 //
 // The array lives for as long as the library is loaded, on every GPU that
 // loads it: kNoAllocScratchBytes (64 MiB) per device. Problems whose split

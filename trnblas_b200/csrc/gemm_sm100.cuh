@@ -189,6 +189,24 @@ struct GemmCfg {
 // cycles.
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz, int& mb, int& nb);
 
+// K blocks this CTA runs over all its tiles: my_tiles * num_kb, or for a
+// triangular operand the sum of the tiles' K ranges (every role that walks
+// the stage stream counts the same stages).
+__device__ __forceinline__ long long cta_stage_total(const GemmParams& p, int bm, int bn, int bk,
+                                                     int num_kb) {
+  const int my_tiles =
+      p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (!p.tri) return static_cast<long long>(my_tiles) * num_kb;
+  long long total = 0;
+  for (int ti = 0; ti < my_tiles; ++ti) {
+    int bz, mb, nb, lo, hi;
+    decode_tile(p, static_cast<int>(blockIdx.x) + ti * static_cast<int>(gridDim.x), bz, mb, nb);
+    tile_k_range(p, mb * bm, bm, nb * bn, bn, bk, num_kb, lo, hi);
+    total += hi - lo;
+  }
+  return total;
+}
+
 template <int KIND, int BN, int STAGES>
 __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem,
                                               uint64_t* full_bar, uint64_t* empty_bar,
@@ -230,11 +248,7 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
     tile_k_range(p, mb * Cfg::BM, Cfg::BM, nb * BN, BN, Cfg::BK, num_kb, lo, hi);
     return hi - lo;
   };
-  long long total = static_cast<long long>(my_tiles) * num_kb;
-  if (p.tri) {
-    total = 0;
-    for (int ti = 0; ti < my_tiles; ++ti) total += tile_kb(ti);
-  }
+  const long long total = cta_stage_total(p, Cfg::BM, BN, Cfg::BK, num_kb);
   int ti = 0;
   int cnt = my_tiles > 0 ? tile_kb(0) : 0;  // K blocks of the current tile
   uint32_t phase = 0;
@@ -678,9 +692,7 @@ __global__ void __launch_bounds__(GemmCfg<KIND, BN>::THREADS, 1)
     // split is elementwise). inf / nan keep lo = 0.
     constexpr int CT = 32 * Cfg::CONV_WARPS;
     const int ct = threadIdx.x - 192;  // 0 .. CT - 1
-    const int my_tiles =
-        p.num_tiles > static_cast<int>(blockIdx.x) ? (p.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const long long total = static_cast<long long>(my_tiles) * num_kb;
+    const long long total = cta_stage_total(p, BM, BN, BK, num_kb);
     int stage = 0;
     uint32_t phase = 0;
     for (long long g = 0; g < total; ++g) {

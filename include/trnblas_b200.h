@@ -211,15 +211,15 @@ TRNBLAS_API size_t trnblas_pair_energy_workspace_size(int64_t nocc, int64_t nvir
  *   E = sum_p w_p sum_{a,b} T_ab (2 T_ab - T_ba) / (e_i + e_j - e_a - e_b),
  *   T = B_i B_j^T (nvir x nvir, contracted over naux), w_p = 1 (i == j) or 2.
  * B is (nocc, nvir, naux) fp32 contiguous, eps fp32. B is split per row
- * (i, a) into int8 digit planes with a power-of-two exponent: for naux <=
- * 33280, 4 base-254 digits with the slice products of diagonals <= 3 (10
- * products) and the diagonal elements of the i == j pairs from exact fp64
- * row sums of squares; for 33280 < naux <= 104857, 5 balanced 7-bit digits
- * with diagonals <= 4 (15 products). T is formed tile by tile from exact
- * int32 diagonal sums in TMEM and reduced in the epilogue (fp64 sums); it
- * never reaches HBM. The fp64 result is written to *energy (device pointer).
- * Deterministic. Workspace holds two copies of the digit planes: about
- * 8 (or 10) * nocc * nvir * naux bytes.
+ * (i, a) into 4 int8 base-254 digit planes with a power-of-two exponent; T
+ * keeps the slice products of diagonals <= 3 (10 products), the diagonal
+ * elements of the i == j pairs come from exact fp64 row sums of squares. T is
+ * formed tile by tile from exact int32 diagonal sums in TMEM (K chunks of at
+ * most 33280 naux, whose folds are added in fp64) and reduced in the
+ * epilogue in fp64; it never reaches HBM. naux <= 2^30. The fp64 result is
+ * written to *energy (device pointer). Deterministic. Workspace holds the
+ * digit planes once: about 4 * nocc * round_up(nvir, 128) * round_up(naux,
+ * 64) bytes.
  * Replaces trnblas/nki/dispatch.py:2537-2569 (nki_batched_pair_energy),
  * :2768-2795 (_nki_pair_energy_sym_impl), trnblas/nki/multicore.py:212-289
  * (sym_rows / aten_rows) and the NKI kernel dispatch.py:4900-5001

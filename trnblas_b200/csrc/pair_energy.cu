@@ -34,9 +34,7 @@
 namespace tb {
 
 struct PairParams {
-  const int8_t* digA;      // digits in 128-row blocks (A operand), rows (i, a) at i * nv_pad + a
-  const int8_t* digB;      // the same digits in 64-row blocks (B operand)
-  long long rows_pad;      // nocc * nv_pad
+  long long rows_pad;      // nocc * nv_pad (digit rows (i, a) at i * nv_pad + a)
   int nv_pad;              // nvir rounded up to 128 (zero rows beyond nvir)
   int nocc, nvir, naux_p;  // naux_p: K columns of the digit planes (multiple of the stage K)
   long long pair_begin;
@@ -130,7 +128,7 @@ constexpr int kMaxGrid = 1024;
 struct PairLayout {
   long long naux_p, R, nv_pad, rows_pad;
   int slices;
-  size_t off_digb, off_exps, off_max, off_range, off_rowsq, off_part, off_order, total;
+  size_t off_exps, off_max, off_range, off_rowsq, off_part, off_order, total;
 };
 
 PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long npairs) {
@@ -140,10 +138,9 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long
   L.R = nocc * nvir;
   L.nv_pad = round_up(std::max<long long>(nvir, 1), 128);
   L.rows_pad = nocc * L.nv_pad;
-  // the digits twice: in 128-row blocks (A operand) and in 64-row blocks (B)
+  // the digits (pe_digit_offset), read by both MMA operands
   const size_t dig = static_cast<size_t>(round_up(L.slices * L.rows_pad * L.naux_p, 256));
-  L.off_digb = dig;
-  L.off_exps = 2 * dig;
+  L.off_exps = dig;
   L.off_max = L.off_exps + round_up(4 * L.R, 256);
   L.off_range = L.off_max + round_up(8 * L.R, 256);
   L.off_rowsq = L.off_range + 256;
@@ -154,12 +151,12 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long
 }
 
 // Pair-block width g of the processing order: the digits of 2g occupied
-// orbitals (both layouts) should fit in half of L2.
+// orbitals should fit in half of L2.
 int pair_block(const PairLayout& L, long long nocc) {
   int l2 = 0;
   if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, current_device()) != cudaSuccess || l2 <= 0)
     l2 = 96 << 20;
-  const double per_orb = 2.0 * L.slices * static_cast<double>(L.nv_pad) * L.naux_p;
+  const double per_orb = static_cast<double>(L.slices) * static_cast<double>(L.nv_pad) * L.naux_p;
   const long long g = static_cast<long long>(0.5 * l2 / (2.0 * per_orb));
   return static_cast<int>(std::max<long long>(1, std::min<long long>(g, std::max<long long>(nocc, 1))));
 }
@@ -236,14 +233,13 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int8_t* dig = reinterpret_cast<int8_t*>(ws);
-  int8_t* digb = reinterpret_cast<int8_t*>(ws + L.off_digb);
   int* exps = reinterpret_cast<int*>(ws + L.off_exps);
   SplitScratch sc{reinterpret_cast<unsigned long long*>(ws + L.off_max),
                   reinterpret_cast<int*>(ws + L.off_range)};
   double* partials = reinterpret_cast<double*>(ws + L.off_part);
   int2* order = reinterpret_cast<int2*>(ws + L.off_order);
   double* rowsq = reinterpret_cast<double*>(ws + L.off_rowsq);
-  // per-row exponents and sums of squares, then the base-254 digits in both layouts
+  // per-row exponents and sums of squares, then the base-254 digits
   cudaError_t e = cudaSuccess;
   {
     const int R = static_cast<int>(L.R);
@@ -260,7 +256,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
     const long long g3 = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
     pe254_digits_kernel<<<static_cast<unsigned>(g3), dim3(32, 8), 0, stream>>>(
         B, static_cast<int>(naux), static_cast<int>(nvir), static_cast<int>(L.nv_pad), L.rows_pad,
-        static_cast<int>(L.naux_p), exps, dig, digb);
+        static_cast<int>(L.naux_p), exps, dig);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return cuda_fail(e, "pair energy split launch");
@@ -274,9 +270,25 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
         pair_begin, pair_end, g, order);
   }
 
+  // The digits as a 5-D tensor: bytes of a 256-byte row, the 16 rows of one
+  // plane of a 64-row block, row blocks, planes, K superslabs; the A operand
+  // reads two row blocks at a time, the B operand one.
+  CUtensorMap map_a, map_b;
+  {
+    const uint64_t nblk = static_cast<uint64_t>(L.rows_pad / 64);
+    const uint64_t dims[5] = {256, 16, nblk, static_cast<uint64_t>(Pe254::KS),
+                              static_cast<uint64_t>(L.naux_p / Pe254::SW)};
+    const uint64_t strides[4] = {256, 4096, nblk * 4096, Pe254::KS * nblk * 4096};
+    const uint32_t box_a[5] = {256, 16, 2, Pe254::KS, 1};
+    const uint32_t box_b[5] = {256, 16, 1, Pe254::KS, 1};
+    if (!encode_map(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 5, dims, strides, box_a,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_map(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dig, 5, dims, strides, box_b,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+      return TRNBLAS_ERR_ALIGN;
+  }
+
   PairParams p{};
-  p.digA = dig;
-  p.digB = digb;
   p.rows_pad = L.rows_pad;
   p.nv_pad = static_cast<int>(L.nv_pad);
   p.nocc = static_cast<int>(nocc);
@@ -305,7 +317,7 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair energy smem)");
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    pair_energy254_kernel<<<grid, Pe254::THREADS, Pe254::SMEM, stream>>>(p);
+    pair_energy254_kernel<<<grid, Pe254::THREADS, Pe254::SMEM, stream>>>(p, map_a, map_b);
   }
   pair_energy_finish<<<1, 32, 0, stream>>>(partials, grid, energy);
   e = cudaGetLastError();

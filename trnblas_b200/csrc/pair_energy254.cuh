@@ -36,46 +36,25 @@
 // factor 1 / 127^4 is applied once per thread.
 //
 // Pipeline. One stage holds a 64-wide K superslab of all 4 planes of the
-// 128-row A block (32 KB) and of the 64-row B block (16 KB), each ONE bulk
-// copy (the digits are stored in that image, `sblocked_offset`): about 640
-// cycles of the SM's copy engine against ~670 of MMA per stage. TMEM holds
-// two pass buffers of 4 x 64 columns (X in buffer 0, Y in buffer 1: all 512
-// columns), so the MMA runs the next pass while the epilogue folds the last.
+// 128-row A block (32 KB) and of the 64-row B block (16 KB), each ONE TMA
+// tensor copy out of the single digit layout (pe_digit_offset), whose boxes
+// land in shared memory as the MMA's no-swizzle images. (An earlier layout
+// stored the digits twice, in 128-row and in 64-row blocks, so that each
+// operand was one contiguous bulk copy: twice the digit bytes in HBM and in
+// L2.) TMEM holds two pass buffers of 4 x 64 columns (X in buffer 0, Y in
+// buffer 1: all 512 columns), so the MMA runs the next pass while the
+// epilogue folds the last.
 #pragma once
 
 #include "ozaki_split.cuh"
 
 namespace tb {
 
-// Superslab blocked digit layout: [K superslab of 2^sw_log2][row block of
-// 2^rb_log2 rows][plane][8-row group][16-byte K chunk][row in group (8)]
-// [16 bytes]. All planes of one row block of one superslab form one chunk;
-// inside a plane the K-major no-swizzle core matrices sit LBO = 128 bytes
-// apart along K and SBO = 2^sw_log2 * 8 bytes apart along the rows.
-__host__ __device__ __forceinline__ long long sblocked_offset(long long p, int k, int s, int slices,
-                                                              long long rows_pad, int rb_log2,
-                                                              int sw_log2) {
-  const long long ss = k >> sw_log2;
-  const int kk = k & ((1 << sw_log2) - 1);
-  const long long nblk = rows_pad >> rb_log2;
-  const long long blk = p >> rb_log2;
-  const long long grp = (p & ((1ll << rb_log2) - 1)) >> 3;
-  const long long plane = (ss * nblk + blk) * slices + s;
-  return (plane << (rb_log2 + sw_log2)) + (((grp << (sw_log2 - 4)) + (kk >> 4)) << 7) +
-         ((p & 7) << 4) + (kk & 15);
-}
-
-__host__ __device__ __forceinline__ long long sblocked_chunk(long long ss, long long blk, int slices,
-                                                             long long rows_pad, int rb_log2,
-                                                             int sw_log2) {
-  return ((ss * (rows_pad >> rb_log2) + blk) * slices) << (rb_log2 + sw_log2);
-}
-
 struct Pe254 {
   static constexpr int KS = 4;    // digit planes
   static constexpr int DMAX = 3;  // diagonals s + t <= DMAX are kept
   static constexpr int BM = 128, BN = 64;
-  static constexpr int SW_LOG2 = 6, SW = 1 << SW_LOG2;  // K per stage
+  static constexpr int SW = 64;   // K per stage (one superslab of the digit layout)
   static constexpr int A_PLANE = BM * SW, B_PLANE = BN * SW;
   static constexpr int A_OFF = 0, B_OFF = KS * A_PLANE;
   static constexpr int STAGE_BYTES = KS * (A_PLANE + B_PLANE);
@@ -89,6 +68,25 @@ struct Pe254 {
   static constexpr int CH_KB = CHUNK_NAUX / SW;     // stages of one exact int32 chunk
   static_assert(2 * ACC_COLS <= 512, "two pass buffers in TMEM");
 };
+
+// Digit layout, one copy serving both MMA operands: [K superslab of 64]
+// [plane][64-row block][8-row group][16-byte K chunk (4)][row in group (8)]
+// [16 bytes]. One plane of one row block is 4 KB; inside it the K-major
+// no-swizzle core matrices sit LBO = 128 bytes apart along K and SBO = 512
+// bytes apart along the rows. The kernel reads it through a 5-D tensor map
+// (bytes of a 256-byte row, the 16 such rows of a plane block, row blocks,
+// planes, superslabs): the A operand (128 rows) as the box {256, 16, 2, 4, 1},
+// which lands in shared memory as [plane][2 row blocks][4 KB], i.e. 8 KB
+// planes whose 16 row groups are SBO apart; the B operand (64 rows) as
+// {256, 16, 1, 4, 1}, i.e. [plane][4 KB], the planes stacked along N with the
+// same SBO. Offset of plane 0 of padded row p at K index k (plane s adds
+// s * nblk * 4096; nblk = padded rows / 64):
+__host__ __device__ __forceinline__ long long pe_digit_offset(long long p, int k, long long nblk) {
+  const long long ss = k >> 6;
+  const int kk = k & 63;
+  return ((ss * Pe254::KS * nblk + (p >> 6)) << 12) + (((((p >> 3) & 7) << 2) + (kk >> 4)) << 7) +
+         ((p & 7) << 4) + (kk & 15);
+}
 
 // Per-row statistics of B (R rows of naux fp32, contiguous): max |x| as IEEE
 // bits (for the exponent) and the fp64 sum of squares, one warp per row,
@@ -129,15 +127,14 @@ __global__ void __launch_bounds__(256)
 }
 
 // Base-254 digits of B (nocc * nvir rows of naux fp32, row (i, a) at
-// i * nvir + a) into the superslab layout twice: 128-row blocks (digA, the A
-// operand) and 64-row blocks (digB); padded row p = i * nv_pad + a, zero for
-// a >= nvir and k >= naux. 32 x 32 tiles through a cp.async ring (persistent
-// grid), each thread 4 consecutive K of one row, one 32-bit store per plane
-// and layout.
+// i * nvir + a) into the digit layout (pe_digit_offset); padded row
+// p = i * nv_pad + a, zero for a >= nvir and k >= naux. 32 x 32 tiles through
+// a cp.async ring (persistent grid), each thread 4 consecutive K of one row,
+// one 32-bit store per plane.
 __global__ void __launch_bounds__(256)
     pe254_digits_kernel(const float* __restrict__ B, int naux, int nvir, int nv_pad,
                         long long rows_pad, int naux_p, const int* __restrict__ exps,
-                        int8_t* __restrict__ digA, int8_t* __restrict__ digB) {
+                        int8_t* __restrict__ dig) {
   __shared__ __align__(16) float tile[kOzBuf][32][33];
   const int tx = threadIdx.x, ty = threadIdx.y, t = ty * 32 + tx;
   const int nslab = naux_p / 32;
@@ -182,8 +179,8 @@ __global__ void __launch_bounds__(256)
     double u[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) u[e] = static_cast<double>(tile[buf][crow][kq + e]) * f;  // exact
-    int8_t* outA = digA + sblocked_offset(p, k0 + kq, 0, Pe254::KS, rows_pad, 7, Pe254::SW_LOG2);
-    int8_t* outB = digB + sblocked_offset(p, k0 + kq, 0, Pe254::KS, rows_pad, 6, Pe254::SW_LOG2);
+    const long long nblk = rows_pad >> 6;
+    int8_t* out = dig + pe_digit_offset(p, k0 + kq, nblk);
 #pragma unroll
     for (int s = 0; s < Pe254::KS; ++s) {
       int d[4];
@@ -197,8 +194,7 @@ __global__ void __launch_bounds__(256)
       }
       const uint32_t w = __byte_perm(__byte_perm(d[0], d[1], 0x0040), __byte_perm(d[2], d[3], 0x0040),
                                      0x5410);
-      *reinterpret_cast<uint32_t*>(outA + s * Pe254::A_PLANE) = w;
-      *reinterpret_cast<uint32_t*>(outB + s * Pe254::B_PLANE) = w;
+      *reinterpret_cast<uint32_t*>(out + s * (nblk << 12)) = w;
     }
   }
   cp_async_wait<0>();
@@ -278,7 +274,9 @@ __device__ __forceinline__ void pe254_mma_role(uint8_t* smem, uint64_t* full_bar
 
 // Block: warp 0 producer, warp 1 MMA issuer and TMEM owner, warps 2..17
 // epilogue (four per TMEM lane quarter, 16 columns of the 64 each).
-__global__ void __launch_bounds__(Pe254::THREADS, 1) pair_energy254_kernel(const PairParams p) {
+__global__ void __launch_bounds__(Pe254::THREADS, 1)
+    pair_energy254_kernel(const PairParams p, const __grid_constant__ CUtensorMap map_a,
+                          const __grid_constant__ CUtensorMap map_b) {
   using C = Pe254;
   constexpr int STAGES = C::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -324,6 +322,8 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1) pair_energy254_kernel(const
     int stage = 0;
     uint32_t phase = 0;
     bool aborted = false;
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
       int i, j, R, Cb;
       unit_of(p, u, i, j, R, Cb);
@@ -339,12 +339,9 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1) pair_energy254_kernel(const
           }
           uint8_t* st = smem + stage * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
-          bulk_load(st + C::A_OFF,
-                    p.digA + sblocked_chunk(kb, ra >> 7, C::KS, p.rows_pad, 7, C::SW_LOG2),
-                    C::KS * C::A_PLANE, &full_bar[stage]);
-          bulk_load(st + C::B_OFF,
-                    p.digB + sblocked_chunk(kb, rb >> 6, C::KS, p.rows_pad, 6, C::SW_LOG2),
-                    C::KS * C::B_PLANE, &full_bar[stage]);
+          // row blocks of 64: A rows ra .. ra + 127 (two blocks), B rows rb .. rb + 63
+          tma_load_5d(st + C::A_OFF, &map_a, &full_bar[stage], 0, 0, static_cast<int>(ra >> 6), 0, kb);
+          tma_load_5d(st + C::B_OFF, &map_b, &full_bar[stage], 0, 0, static_cast<int>(rb >> 6), 0, kb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;

@@ -496,7 +496,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
             "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
             "peak_source": f"{src} {'bf16 sustained' if dtype == torch.bfloat16 else 'bf16 sustained / 6 (3 tf32 products at half the bf16 rate)'}",
-            "kernel": "gemm_sm100_kernel",
+            "kernel": "gemm_pair_kernel (CTA pairs, 256 x 256 tiles)" + ("" if dtype == torch.bfloat16 else " after the split pass"),
             "kernel_ms": round(kern_ms, 4),
             "traffic": TRAFFIC.get(f"spmd_{'bf16' if dtype == torch.bfloat16 else 'fp32'}_{pr}x{pc}"),
         },

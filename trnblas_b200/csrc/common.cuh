@@ -139,6 +139,22 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
   return ok != 0;
 }
 
+// Soft wave barrier of a persistent work walk: the producer waits until
+// every CTA has issued the loads of its previous work item (`target`
+// arrivals on the launch's counter), so the CTAs start their items together
+// and read the operand slabs they share while those are still in L2 (left
+// alone, CTAs drift apart over a long K loop and each re-reads from DRAM what
+// the others loaded). Only a performance hint: after `limit_ns` the producer goes
+// on regardless, so a CTA that is not resident cannot hold the others up.
+__device__ __forceinline__ void soft_wave_wait(const int* ctr, int target,
+                                               unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (*reinterpret_cast<const volatile int*>(ctr) < target) {
+    if (globaltimer_ns() - t0 > limit_ns) break;
+    __nanosleep(128);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------
@@ -366,6 +382,16 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -229,11 +229,13 @@ int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
 
 // The CTA-pair kernel: clusters of two CTAs, as many pairs as can be
 // resident at once (the persistent tile walk needs every pair running).
-template <int STAGES>
-int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, cudaStream_t stream) {
-  using Cfg = PairGemmCfg<STAGES>;
+// a1 / b1: the lo planes of the split pass for kTF32x3 (pass a / b again for kF16).
+template <int KIND, int STAGES>
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& a1, const CUtensorMap& b,
+                     const CUtensorMap& b1, GemmParams& p, cudaStream_t stream) {
+  using Cfg = PairGemmCfg<KIND, STAGES>;
   constexpr int smem = Cfg::SMEM;
-  auto kern = gemm_pair_kernel<STAGES>;
+  auto kern = gemm_pair_kernel<KIND, STAGES>;
   static int max_pairs[64] = {};
   const int dev = current_device();
   cudaLaunchConfig_t cfg{};
@@ -242,7 +244,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, 
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -264,7 +266,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, GemmParams& p, 
   const int pairs = static_cast<int>(std::min<long long>(p.num_tiles, max_pairs[dev]));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   if (use_wave_sync(p.K, p.num_tiles, pairs)) p.wave_ctr = wave_counter(stream);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, a1, b, b1, p);
   if (e != cudaSuccess) return cuda_fail(e, "pair gemm kernel launch");
   return TRNBLAS_OK;
 }
@@ -541,6 +543,15 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     p.a_mn = 0;
     p.b_mn = 0;
     p.in_fmt = kFmtTF32;
+    if (use_pair_gemm(M, N)) {
+      // 256 x 256 tiles on CTA pairs: each CTA reads half the shared-memory
+      // bytes per MMA of a 128 x 128 tile
+      p.group_m = group_m_override() ? group_m_override() : 8;
+      p.tiles_m = static_cast<int>(ceil_div(M, 256));
+      p.tiles_n = static_cast<int>(ceil_div(N, 256));
+      p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
+      return launch_gemm_pair<kTF32x3, 3>(ma0, ma1, mb0, mb1, p, stream);
+    }
     p.tiles_m = static_cast<int>(ceil_div(M, 128));
     p.tiles_n = static_cast<int>(ceil_div(N, 128));
     p.num_tiles = static_cast<int>(batch * p.tiles_m * p.tiles_n);
@@ -572,7 +583,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
       p.shard_tiles_m = static_cast<int>(rs->shard_rows / 256);
       p.rot_m = static_cast<int>(rs->rot_rows / 256) % p.tiles_m;
     }
-    return launch_gemm_pair<6>(ma0, mb0, p, stream);
+    return launch_gemm_pair<kF16, 6>(ma0, ma0, mb0, mb0, p, stream);
   }
   const int bn = pick_bn(batch, M, N);
   bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)

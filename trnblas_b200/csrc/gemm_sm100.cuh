@@ -121,22 +121,6 @@ __device__ __forceinline__ bool wait_ready(const int* flag, int epoch, const Abo
   return true;
 }
 
-// Soft wave barrier of the persistent tile walk: the producer waits until
-// every CTA has issued the loads of its previous tile (`target` arrivals on
-// the launch's counter), so the CTAs of a wave start their tiles together and
-// read the operand slabs they share while those are still in L2 (left alone,
-// CTAs drift apart over a long K loop and each re-reads from DRAM what the
-// others loaded). Only a performance hint: after `limit_ns` the producer goes
-// on regardless, so a CTA that is not resident cannot hold the others up.
-__device__ __forceinline__ void soft_wave_wait(const int* ctr, int target,
-                                               unsigned long long limit_ns) {
-  const unsigned long long t0 = globaltimer_ns();
-  while (*reinterpret_cast<const volatile int*>(ctr) < target) {
-    if (globaltimer_ns() - t0 > limit_ns) break;
-    __nanosleep(128);
-  }
-}
-
 // x - trunc19(x): the part of x below the 19 bits a kind::tf32 operand keeps
 // (exact in fp32); 0 for inf / nan.
 __device__ __forceinline__ float tf32_lo(float x) {
@@ -454,38 +438,48 @@ __device__ __forceinline__ void syrk_mirror_block(const GemmParams& p, long long
 // Epilogue for one 32-column chunk held by this thread: row r (global), columns
 // c0 .. c0+31 (global), accumulator values v[0..31]. `tsm`: this warp's 4 KB
 // shared-memory stage (SYRK mirror).
+// GEMM epilogue of 32 consecutive columns c0 .. of row r: alpha * acc
+// (+ beta * C), stored in the output type.
+__device__ __forceinline__ void epilogue_row32(const GemmParams& p, int bz, int r, int c0,
+                                               const float* v) {
+  const long long dbase = static_cast<long long>(bz) * p.strideD;
+  const long long cbase = static_cast<long long>(bz) * p.strideC;
+  const bool has_c = (p.c_mode != kCNone) && (p.beta != 0.0f);
+  if (r >= p.M) return;
+  float out[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
+  const bool full = (c0 + 32 <= p.N);
+  if (has_c) {
+    const long long crow = cbase + static_cast<long long>(r) * p.ldc;
+    if (full && p.out_kind == kOutF32 && (p.ldc % 4 == 0) &&
+        ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((cbase & 3) == 0)) {
+      const float4* cp = reinterpret_cast<const float4*>(
+          reinterpret_cast<const float*>(p.C) + crow + c0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 c4 = __ldg(cp + j);
+        out[4 * j + 0] += p.beta * c4.x;
+        out[4 * j + 1] += p.beta * c4.y;
+        out[4 * j + 2] += p.beta * c4.z;
+        out[4 * j + 3] += p.beta * c4.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < p.N) out[j] += p.beta * load_c(p.C, p.out_kind, crow + c0 + j);
+    }
+  }
+  store_row32(p, dbase + static_cast<long long>(r) * p.ldd, c0, out, full);
+}
+
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int bz, int r, int c0,
                                                const float* v, bool diag_tile, void* tsm) {
   const long long dbase = static_cast<long long>(bz) * p.strideD;
   const long long cbase = static_cast<long long>(bz) * p.strideC;
   const bool has_c = (p.c_mode != kCNone) && (p.beta != 0.0f);
   if (p.mode == kModeGemm) {
-    if (r >= p.M) return;
-    float out[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
-    const bool full = (c0 + 32 <= p.N);
-    if (has_c) {
-      const long long crow = cbase + static_cast<long long>(r) * p.ldc;
-      if (full && p.out_kind == kOutF32 && (p.ldc % 4 == 0) &&
-          ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((cbase & 3) == 0)) {
-        const float4* cp = reinterpret_cast<const float4*>(
-            reinterpret_cast<const float*>(p.C) + crow + c0);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 c4 = __ldg(cp + j);
-          out[4 * j + 0] += p.beta * c4.x;
-          out[4 * j + 1] += p.beta * c4.y;
-          out[4 * j + 2] += p.beta * c4.z;
-          out[4 * j + 3] += p.beta * c4.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < p.N) out[j] += p.beta * load_c(p.C, p.out_kind, crow + c0 + j);
-      }
-    }
-    store_row32(p, dbase + static_cast<long long>(r) * p.ldd, c0, out, full);
+    epilogue_row32(p, bz, r, c0, v);
     return;
   }
   // SYRK: lower element (r, c) with r >= c, mirrored to (c, r).

@@ -25,6 +25,7 @@
 // X(2X-Y) / D once; a in block 2R+1 with b in block 2R is skipped (unit
 // (R, 2R+1) counted it). The nvir x nvir T never reaches HBM.
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <string>
 
@@ -47,6 +48,8 @@ struct PairParams {
   const float* eps_occ;
   const float* eps_vir;
   double* partials;        // gridDim.x
+  int* wave_ctr;           // soft wave synchronisation counter (nullptr: none)
+  int sync_kb, sync_lag;   // its group length (stages) and lag (groups)
   int* status;
   unsigned long long timeout_ns;
 };
@@ -150,12 +153,17 @@ PairLayout pair_layout(long long nocc, long long nvir, long long naux, long long
   return L;
 }
 
-// Pair-block width g of the processing order: the digits of 2g occupied
-// orbitals should fit in half of L2.
-int pair_block(const PairLayout& L, long long nocc) {
+double l2_bytes() {
   int l2 = 0;
   if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, current_device()) != cudaSuccess || l2 <= 0)
     l2 = 96 << 20;
+  return static_cast<double>(l2);
+}
+
+// Pair-block width g of the processing order: the digits of 2g occupied
+// orbitals should fit in half of L2.
+int pair_block(const PairLayout& L, long long nocc) {
+  const double l2 = l2_bytes();
   const double per_orb = static_cast<double>(L.slices) * static_cast<double>(L.nv_pad) * L.naux_p;
   const long long g = static_cast<long long>(0.5 * l2 / (2.0 * per_orb));
   return static_cast<int>(std::max<long long>(1, std::min<long long>(g, std::max<long long>(nocc, 1))));
@@ -167,6 +175,27 @@ void host_pair_of(long long p, int& i, int& j) {
   while ((jj + 1) * (jj + 2) / 2 <= p) ++jj;
   j = static_cast<int>(jj);
   i = static_cast<int>(p - jj * (jj + 1) / 2);
+}
+
+// Soft wave synchronisation of the pair walk (pe254_group_target): group
+// length in stages (TRNBLAS_B200_PAIR_SYNC, 0 = off) and lag in groups
+// (TRNBLAS_B200_PAIR_SYNC_LAG). Measured at config 5b (96 / 2208 / 6912) on
+// one box: group length 8 / 16 / 32 / 64 stages 1745 / 1646 / 1600 / 1601 ms
+// a launch (lags 1 and 2 no better than 0); without it 2.29-2.35 s on
+// another box that took 1.48 s with 16-stage groups. Used only when the
+// digits outgrow L2 (below that they stay resident whatever the order;
+// config 3's 113 MB: no change either way).
+int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+int pair_sync_kb() {
+  static const int v = env_int("TRNBLAS_B200_PAIR_SYNC", 32);
+  return v > 0 ? v : 0;
+}
+int pair_sync_lag() {
+  static const int v = env_int("TRNBLAS_B200_PAIR_SYNC_LAG", 0);
+  return v > 0 ? v : 0;
 }
 
 int units_per_pair(long long nvir) {
@@ -305,6 +334,11 @@ int trnblas_pair_energy(int64_t nocc, int64_t nvir, int64_t naux, const float* B
   p.eps_occ = eps_occ;
   p.eps_vir = eps_vir;
   p.partials = partials;
+  p.sync_kb = pair_sync_kb();
+  p.sync_lag = pair_sync_lag();
+  p.wave_ctr = (p.sync_kb > 0 && static_cast<double>(L.off_exps) > l2_bytes()) ? wave_counter(stream)
+                                                                                 : nullptr;
+  if (!p.wave_ctr) p.sync_kb = 1;  // unused; keeps the producer's modulo defined
   p.status = status;
   p.timeout_ns = wait_timeout_ns();
 

@@ -88,6 +88,29 @@ __host__ __device__ __forceinline__ long long pe_digit_offset(long long p, int k
          ((p & 7) << 4) + (kk & 15);
 }
 
+// Soft wave synchronisation of the pair walk. Every CTA's stream of stages
+// (its units x 2 passes x num_kb) is cut into groups of sync_kb stages; after
+// issuing a group the producer adds 1 to the launch's counter, and before
+// issuing group g it waits (a hint, at most 100 us) until every CTA has
+// issued its groups before g - sync_lag. The CTAs then stream the same K range of the
+// concurrently processed units together, so an operand block shared by many
+// CTAs (one A block feeds ~30 units of a pair, one B block ~5) is read once
+// from DRAM while it sits in L2: measured at config 5b (96 / 2208 / 6912),
+// the free-running CTAs drifted apart and read 9.34 TB from DRAM per launch
+// (60 % of the 15.7 TB the SMs load), most of the kernel's power under the
+// 1 kW cap. Counter value once every CTA has issued groups 0 .. g - 1: CTAs
+// hold (units of CTA b) = q + (b < r) units for q, r = num_units / grid,
+// num_units % grid, and so ceil(units * 2 * num_kb / sync_kb) groups.
+__device__ __forceinline__ int pe254_group_target(long long num_units, int grid, int num_kb,
+                                                  int sync_kb, int g) {
+  const long long q = num_units / grid, r = num_units % grid;
+  const long long per_unit = 2ll * num_kb;
+  const long long g_hi = ((q + 1) * per_unit + sync_kb - 1) / sync_kb;
+  const long long g_lo = (q * per_unit + sync_kb - 1) / sync_kb;
+  const long long t = r * (g < g_hi ? g : g_hi) + (grid - r) * (g < g_lo ? g : g_lo);
+  return static_cast<int>(t < 0x7fffffffll ? t : 0x7fffffffll);
+}
+
 // Per-row statistics of B (R rows of naux fp32, contiguous): max |x| as IEEE
 // bits (for the exponent) and the fp64 sum of squares, one warp per row,
 // reduced in a fixed order (deterministic).
@@ -324,6 +347,7 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
     bool aborted = false;
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
+    long long gs = 0;  // stages issued (position in this CTA's stream)
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
       int i, j, R, Cb;
       unit_of(p, u, i, j, R, Cb);
@@ -332,7 +356,12 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
       for (int pass = 0; pass < 2 && !aborted; ++pass) {
         const long long ra = (pass == 0 ? ri : rj) + 128 * R;  // A rows: B_i[R] then B_j[R]
         const long long rb = (pass == 0 ? rj : ri) + 64 * Cb;  // B rows: B_j[C] then B_i[C]
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb, ++gs) {
+          if (p.wave_ctr && gs % p.sync_kb == 0 && gs / p.sync_kb > p.sync_lag)
+            soft_wave_wait(p.wave_ctr,
+                           pe254_group_target(p.num_units, gridDim.x, num_kb, p.sync_kb,
+                                              static_cast<int>(gs / p.sync_kb) - p.sync_lag),
+                           100000ull);
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, ab, kTimeoutEmpty)) {
             aborted = true;
             break;
@@ -342,6 +371,9 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
           // row blocks of 64: A rows ra .. ra + 127 (two blocks), B rows rb .. rb + 63
           tma_load_5d(st + C::A_OFF, &map_a, &full_bar[stage], 0, 0, static_cast<int>(ra >> 6), 0, kb);
           tma_load_5d(st + C::B_OFF, &map_b, &full_bar[stage], 0, 0, static_cast<int>(rb >> 6), 0, kb);
+          if (p.wave_ctr && ((gs + 1) % p.sync_kb == 0 ||
+                             (u + gridDim.x >= p.num_units && pass == 1 && kb + 1 == num_kb)))
+            atomicAdd(p.wave_ctr, 1);  // group complete (or this CTA's last, partial one)
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -392,6 +424,30 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
     int it = 0;
     bool aborted = false;
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
+      // The unit's row and column data, loaded before the passes so that
+      // their latency hides behind the MMAs: lane l < 16 holds exps[j][b] and
+      // lane 16 + l exps[i][b] of this warp's column b = b0 + l, lanes < 16
+      // also eps_vir[b] (broadcast to the warp by shuffles in the energy
+      // loop); every lane its own row a's values.
+      int i, j, R, Cb;
+      unit_of(p, u, i, j, R, Cb);
+      const int a = 128 * R + aloc;
+      const int b0 = 64 * Cb + col0;
+      const int bl = b0 + (lane & 15);
+      int e_col = 0;
+      float ev_col = 0.0f;
+      if (bl < p.nvir) {
+        e_col = p.exps[(lane < 16 ? j : i) * p.nvir + bl];
+        ev_col = p.eps_vir[bl];
+      }
+      int eia = 0, eja = 0;
+      float eva = 0.0f;
+      if (a < p.nvir) {
+        eia = p.exps[i * p.nvir + a];
+        eja = p.exps[j * p.nvir + a];
+        eva = p.eps_vir[a];
+      }
+      const float eoi = p.eps_occ[i], eoj = p.eps_occ[j];
       double xt[NCOL], yt[NCOL];
 #pragma unroll
       for (int jj = 0; jj < NCOL; ++jj) xt[jj] = yt[jj] = 0.0;
@@ -428,32 +484,28 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
         }
       }
       if (aborted) break;
-      int i, j, R, Cb;
-      unit_of(p, u, i, j, R, Cb);
-      const int a = 128 * R + aloc;
       // lane mode: 2 = both ordered pairs, 1 = (a, b) once, 0 = skip
       int mode = 2;
       if (Cb == 2 * R + 1) mode = (aloc < 64) ? 2 : 1;
       if (Cb == 2 * R) mode = (aloc < 64) ? 1 : 0;
       if (a >= p.nvir) mode = 0;
       double usum = 0.0;
-      if (mode) {
-        const int eia = p.exps[i * p.nvir + a], eja = p.exps[j * p.nvir + a];
-        const double da = (static_cast<double>(p.eps_occ[i]) + static_cast<double>(p.eps_occ[j])) -
-                          static_cast<double>(p.eps_vir[a]);
-        const int b0 = 64 * Cb + col0;
+      const double da = (static_cast<double>(eoi) + static_cast<double>(eoj)) - static_cast<double>(eva);
 #pragma unroll
-        for (int jj = 0; jj < NCOL; ++jj) {
-          const int b = b0 + jj;
-          if (b < p.nvir) {
-            double X = xt[jj] * pow2d(eia + p.exps[j * p.nvir + b]);
-            double Y = yt[jj] * pow2d(eja + p.exps[i * p.nvir + b]);
-            if (i == j && b == a) X = Y = p.rowsq[i * p.nvir + a] * 16129.0;  // exact T_aa * 127^2
-            const double den = da - static_cast<double>(p.eps_vir[b]);
-            double f = X * (2.0 * X - Y);
-            if (mode == 2) f = fma(Y, 2.0 * Y - X, f);
-            usum += f / den;
-          }
+      for (int jj = 0; jj < NCOL; ++jj) {
+        // every lane takes part in the shuffles; the arithmetic is per lane
+        const int ejb = __shfl_sync(0xffffffffu, e_col, jj);
+        const int eib = __shfl_sync(0xffffffffu, e_col, 16 + jj);
+        const float evb = __shfl_sync(0xffffffffu, ev_col, jj);
+        const int b = b0 + jj;
+        if (mode && b < p.nvir) {
+          double X = xt[jj] * pow2d(eia + ejb);
+          double Y = yt[jj] * pow2d(eja + eib);
+          if (i == j && b == a) X = Y = p.rowsq[i * p.nvir + a] * 16129.0;  // exact T_aa * 127^2
+          const double den = da - static_cast<double>(evb);
+          double f = X * (2.0 * X - Y);
+          if (mode == 2) f = fma(Y, 2.0 * Y - X, f);
+          usum += f / den;
         }
       }
       acc += ((i == j) ? 1.0 : 2.0) * usum;

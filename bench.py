@@ -251,35 +251,30 @@ FLUSHED = ("syrk", "syrk_bf16", "batched_bf16", "gemm1024")
 # None where no capture of the timed shape exists.
 TRAFFIC = {
     "spmd_bf16_1x1": 70950000000,  # profiles/gemm_bf16_32768.md
+    "spmd_fp32_1x1": 281190000000, # profiles/gemm_fp32_32768.md
     "gemm8192_bf16": 1199138448,   # profiles/gemm_bf16_8192.md
-    "gemm8192_fp32": 6728923480,   # profiles/gemm_fp32_8192.md
+    "gemm8192_fp32": 4821362688,   # profiles/gemm_fp32_8192.md
     "batched": 313154560,          # profiles/gemm_batched_64x512.md
     "batched_bf16": 70896640,      # profiles/gemm_batched_bf16.md
     "syrk": 528911104,             # profiles/gemm_syrk_4096.md
     "syrk_bf16": 34854912,         # profiles/gemm_syrk_bf16_4096.md
     "gemm_fp64": 2161969960,       # profiles/ozaki_fp64_4096.md (the int8 GEMM kernel)
-    "pair3": 1991894560,           # profiles/pair_energy_pair3.md
-    "pair5x4": 4592494720,         # profiles/pair_energy_pair5x4.md
+    "pair3": 376285440,            # profiles/pair_energy_pair3.md
+    "pair5x4": 2798001576,         # profiles/pair_energy_pair5x4.md
+    "pair5": 1643160000000,        # profiles/pair_energy_pair5_dram.md
 }
-
-
-# naux above which the pair energy runs its 7-bit form (15 int8 products per
-# 64-column block of T) instead of the base-254 form (10 products)
-PAIR_B254_MAX_NAUX = 33280
 
 
 def pair_int8_ops(npairs: int, nvir: int, naux: int) -> float:
     """int8 ops (2 per multiply-add) the fused pair-energy kernel issues for
     `npairs` pairs: units (128 rows of a x 64 columns of b, C >= 2R) x 2
-    passes x the summed MMA N of one K step (10 or 15 products of 64
-    columns) x 128 rows x the padded naux."""
+    passes x the summed MMA N of one K step (10 base-254 products of 64
+    columns) x 128 rows x naux padded to the 64-wide stage (any naux: longer
+    ones run as K chunks of the same products)."""
     nR, nC = math.ceil(nvir / 128), math.ceil(nvir / 64)
     upp = sum(max(0, nC - 2 * r) for r in range(nR))
-    if naux <= PAIR_B254_MAX_NAUX:
-        prods, naux_p = 10, math.ceil(naux / 64) * 64
-    else:
-        prods, naux_p = 15, math.ceil(naux / 32) * 32
-    return npairs * upp * 2 * prods * 64 * 128 * naux_p * 2.0
+    naux_p = math.ceil(naux / 64) * 64
+    return npairs * upp * 2 * 10 * 64 * 128 * naux_p * 2.0
 
 
 def kernel_avg_ms(events):
@@ -655,7 +650,12 @@ def run_ours(args, rank, world, gpu):
                           steps=min(args.steps, PAIR5_STEPS), warmup=PAIR5_WARMUP)
             line["pair_energy"] = {"metric": pair_metric(96, 2208, 6912), "value": pe["ms_per_step"],
                                    "unit": "ms", "higher_is_better": False,
-                                   "steps": min(args.steps, PAIR5_STEPS), "warmup": PAIR5_WARMUP, **pe}
+                                   "steps": min(args.steps, PAIR5_STEPS), "warmup": PAIR5_WARMUP,
+                                   "roofline": {"bound": "tensor", "achieved": pe["int8_tops_achieved"],
+                                                "peak": pe["int8_peak_tops"], "unit": "TOP/s (int8)",
+                                                "frac": pe["int8_frac"],
+                                                "traffic": TRAFFIC["pair5"] if world == 1 else None},
+                                   **pe}
         if args.workload == "spmd" and not args.no_fp32:
             # config 5a in fp32 (3xTF32), the reference's working precision:
             # its own block, step counts and metric

@@ -77,12 +77,13 @@ def test_both_arms_name_the_same_metric(bench):
 
 
 def test_pair_int8_ops_follow_the_kernel_form(bench):
-    """Config 3 (48/432/1152) runs the base-254 form: 10 products per K step
-    of each 128 x 64 unit; past naux 33280 the 7-bit form's 15."""
+    """The base-254 form: 10 products per K step of each 128 x 64 unit, naux
+    padded to the 64-wide stage; naux past 33280 runs as K chunks of the same
+    products."""
     ops = bench.pair_int8_ops(1176, 432, 1152)
     units = 7 + 5 + 3 + 1
     assert ops == 1176 * units * 2 * 10 * 64 * 128 * 1152 * 2.0
-    assert bench.pair_int8_ops(1, 40, 33281) == 1 * 1 * 2 * 15 * 64 * 128 * 33312 * 2.0
+    assert bench.pair_int8_ops(1, 40, 33281) == 1 * 1 * 2 * 10 * 64 * 128 * 33344 * 2.0
     assert "read_traffic" not in (ROOT / "bench.py").read_text()
 
 

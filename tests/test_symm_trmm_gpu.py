@@ -66,13 +66,14 @@ def test_symm_trmm_bf16_and_large():
 
 
 @pytest.mark.parametrize("dt,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
-def test_trmm_triangle_blocks_every_case(dt, tol):
+@pytest.mark.parametrize("n,m", [(1300, 520), (2600, 1900)])
+def test_trmm_triangle_blocks_every_case(dt, tol, n, m):
     """The GEMM kernel skips the K blocks outside the triangle (triangular
     op(A) on the left, triangular op(B) on the right, lower or upper): every
-    case at a ragged size spanning many K blocks against the fp64 product of
-    the masked triangle."""
+    case at ragged sizes spanning many K blocks against the fp64 product of
+    the masked triangle; 1300 x 520 runs on one-CTA tiles, 2600 x 1900 on
+    CTA pairs (88 pair tiles)."""
     g = torch.Generator(device="cuda").manual_seed(9)
-    n, m = 1300, 520
     A = torch.randn(n, n, device="cuda", generator=g).to(dt)
     for side in ("left", "right"):
         X = torch.randn(*((n, m) if side == "left" else (m, n)), device="cuda", generator=g).to(dt)

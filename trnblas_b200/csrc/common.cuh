@@ -299,6 +299,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -471,6 +479,25 @@ __host__ __device__ constexpr uint32_t idesc(uint32_t acc_fmt, uint32_t a_fmt, u
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
 // 2^n as a double, exact, for n in [-1022, 1023].
+// int32 -> fp64 on the integer and fp64 pipes instead of the conversion
+// unit: the double with high word 0x43300000 and low word v + 2^31 (as
+// unsigned) is 2^52 + 2^31 + v exactly, and subtracting 2^52 + 2^31 is exact.
+__device__ __forceinline__ double i32_to_f64(int v) {
+  return __hiloint2double(0x43300000, v ^ static_cast<int>(0x80000000u)) - 4503601774854144.0;
+}
+
+// 1 / d to within an ulp or two: the hardware's approximate fp64 reciprocal
+// refined by three Newton-Raphson steps r <- r + r (1 - d r) (each squares
+// the relative error). For finite normal d.
+__device__ __forceinline__ double recip_f64(double d) {
+  double r;
+  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(d));
+  r = fma(r, fma(-d, r, 1.0), r);
+  r = fma(r, fma(-d, r, 1.0), r);
+  r = fma(r, fma(-d, r, 1.0), r);
+  return r;
+}
+
 __device__ __forceinline__ double pow2d(int n) {
   return __longlong_as_double(static_cast<long long>(n + 1023) << 52);
 }

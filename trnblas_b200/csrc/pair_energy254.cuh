@@ -435,10 +435,10 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
       const int b0 = 64 * Cb + col0;
       const int bl = b0 + (lane & 15);
       int e_col = 0;
-      float ev_col = 0.0f;
+      float ev_colf = 0.0f;
       if (bl < p.nvir) {
         e_col = p.exps[(lane < 16 ? j : i) * p.nvir + bl];
-        ev_col = p.eps_vir[bl];
+        ev_colf = p.eps_vir[bl];
       }
       int eia = 0, eja = 0;
       float eva = 0.0f;
@@ -462,20 +462,24 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
           tc_fence_after();
           const uint32_t col = lane_base + buf * C::ACC_COLS;
           // one diagonal at a time, smallest first (S_3 / 254^3 + S_2 / 254^2
-          // + S_1 / 254 + S_0), so that only 16 loaded words are live
+          // + S_1 / 254 + S_0), 8 columns a load, so that only 8 loaded words
+          // are live beside the 32 folds
 #pragma unroll
-          for (int d = C::DMAX; d >= 0; --d) {
-            uint32_t v[16];
-            tmem_ld16(col + d * C::BN, v);
-            tmem_ld_wait();
-            const double cd = d == 3 ? c3 : d == 2 ? c2 : d == 1 ? c1 : 1.0;
+          for (int h = 0; h < NCOL / 8; ++h) {
 #pragma unroll
-            for (int jj = 0; jj < NCOL; ++jj) {
-              const double sv = static_cast<double>(static_cast<int>(v[jj]));
-              if (pass == 0)
-                xt[jj] = fma(sv, cd, xt[jj]);
-              else
-                yt[jj] = fma(sv, cd, yt[jj]);
+            for (int d = C::DMAX; d >= 0; --d) {
+              uint32_t v[8];
+              tmem_ld8(col + d * C::BN + 8 * h, v);
+              tmem_ld_wait();
+              const double cd = d == 3 ? c3 : d == 2 ? c2 : d == 1 ? c1 : 1.0;
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const double sv = i32_to_f64(static_cast<int>(v[jj]));
+                if (pass == 0)
+                  xt[8 * h + jj] = fma(sv, cd, xt[8 * h + jj]);
+                else
+                  yt[8 * h + jj] = fma(sv, cd, yt[8 * h + jj]);
+              }
             }
           }
           tc_fence_before();
@@ -491,21 +495,24 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
       if (a >= p.nvir) mode = 0;
       double usum = 0.0;
       const double da = (static_cast<double>(eoi) + static_cast<double>(eoj)) - static_cast<double>(eva);
+      const double ev_col = static_cast<double>(ev_colf);  // one conversion a lane, shuffled below
 #pragma unroll
       for (int jj = 0; jj < NCOL; ++jj) {
         // every lane takes part in the shuffles; the arithmetic is per lane
         const int ejb = __shfl_sync(0xffffffffu, e_col, jj);
         const int eib = __shfl_sync(0xffffffffu, e_col, 16 + jj);
-        const float evb = __shfl_sync(0xffffffffu, ev_col, jj);
+        const double evb = __shfl_sync(0xffffffffu, ev_col, jj);
         const int b = b0 + jj;
         if (mode && b < p.nvir) {
           double X = xt[jj] * pow2d(eia + ejb);
           double Y = yt[jj] * pow2d(eja + eib);
           if (i == j && b == a) X = Y = p.rowsq[i * p.nvir + a] * 16129.0;  // exact T_aa * 127^2
-          const double den = da - static_cast<double>(evb);
+          const double den = da - evb;
           double f = X * (2.0 * X - Y);
           if (mode == 2) f = fma(Y, 2.0 * Y - X, f);
-          usum += f / den;
+          // f / den as f * (1 / den) (den: an orbital-energy difference,
+          // finite and normal); no conversion-unit work but the seed
+          usum = fma(f, recip_f64(den), usum);
         }
       }
       acc += ((i == j) ? 1.0 : 2.0) * usum;

@@ -182,7 +182,10 @@ void host_pair_of(long long p, int& i, int& j) {
 // (TRNBLAS_B200_PAIR_SYNC_LAG). Measured at config 5b (96 / 2208 / 6912) on
 // one box: group length 8 / 16 / 32 / 64 stages 1745 / 1646 / 1600 / 1601 ms
 // a launch (lags 1 and 2 no better than 0); without it 2.29-2.35 s on
-// another box that took 1.48 s with 16-stage groups. Used only when the
+// another box that took 1.48 s with 16-stage groups. In lock-step the MMA
+// waits for its stages ~35-40 % of the time (the CTAs' loads arrive in
+// bursts); neither L2 prefetches of later stages nor per-CTA rotations of
+// the K order changed that (measured, then removed). Used only when the
 // digits outgrow L2 (below that they stay resident whatever the order;
 // config 3's 113 MB: no change either way).
 int env_int(const char* name, int dflt) {

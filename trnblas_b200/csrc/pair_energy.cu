@@ -92,6 +92,20 @@ __global__ void pair_order_kernel(long long begin, long long end, int g, int2* _
   }
 }
 
+// Row block R and column block C of unit u inside its pair (no memory access).
+__device__ __forceinline__ void unit_rc(const PairParams& p, long long u, int& R, int& C) {
+  const long long pr = u / p.units_per_pair;
+  int loc = static_cast<int>(u - pr * p.units_per_pair);
+  R = 0;
+  while (R < p.nR) {
+    const int cnt = p.nC - 2 * R;
+    if (loc < cnt) break;
+    loc -= cnt;
+    ++R;
+  }
+  C = 2 * R + loc;
+}
+
 __device__ __forceinline__ void unit_of(const PairParams& p, long long u, int& i, int& j, int& R,
                                         int& C) {
   const long long pr = u / p.units_per_pair;

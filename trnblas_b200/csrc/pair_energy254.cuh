@@ -348,9 +348,15 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
     long long gs = 0;  // stages issued (position in this CTA's stream)
+    // the pair (i, j) of the next unit is loaded one unit ahead, so that its
+    // latency never holds up the stage ring at a unit boundary
+    int2 ij = p.num_units > blockIdx.x ? p.order[blockIdx.x / p.units_per_pair] : make_int2(0, 0);
     for (long long u = blockIdx.x; u < p.num_units && !aborted; u += gridDim.x) {
-      int i, j, R, Cb;
-      unit_of(p, u, i, j, R, Cb);
+      const long long un = u + gridDim.x;
+      const int2 ij_next = un < p.num_units ? p.order[un / p.units_per_pair] : ij;
+      const int i = ij.x, j = ij.y;
+      int R, Cb;
+      unit_rc(p, u, R, Cb);
       const long long ri = static_cast<long long>(i) * p.nv_pad;
       const long long rj = static_cast<long long>(j) * p.nv_pad;
       for (int pass = 0; pass < 2 && !aborted; ++pass) {
@@ -380,6 +386,7 @@ __global__ void __launch_bounds__(Pe254::THREADS, 1)
           }
         }
       }
+      ij = ij_next;
     }
     if (aborted || ab.raised()) {
       int s = stage;

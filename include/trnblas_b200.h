@@ -113,6 +113,24 @@ TRNBLAS_API int trnblas_gemm_tri(int dtype, int64_t batch, int64_t M, int64_t N,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Symmetric multiply: D = alpha * S @ B + beta * C (side_right = 0; S is
+ * M x M, B is M x N) or alpha * B @ S + beta * C (side_right = 1; S is
+ * N x N), S given by the stored triangle of A (row-major, leading dimension
+ * lda; uplo_lower = 1: the lower triangle, 0: the upper; the other triangle
+ * is never read). B, C, D row-major with their leading dimensions. fp32: the
+ * 3xTF32 split pass reads S from the triangle itself (no full S is formed),
+ * then the GEMM kernel. bf16 / fp16: one pass writes the full S into the
+ * workspace, then the GEMM kernel. Workspace: trnblas_symm_workspace_size.
+ * Replaces the reference's symm (trnblas/level3.py:196-240), which forms the
+ * full symmetric matrix with three elementwise passes before a dense GEMM.
+ */
+TRNBLAS_API size_t trnblas_symm_workspace_size(int dtype, int side_right, int64_t M, int64_t N);
+TRNBLAS_API int trnblas_symm(int dtype, int side_right, int uplo_lower, int64_t M, int64_t N,
+                 float alpha, const void* A, int64_t lda, const void* B, int64_t ldb, float beta,
+                 const void* C, int64_t ldc, void* D, int64_t ldd, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
  * bf16 / fp16 trnblas_gemm (no workspace) whose operands arrive while it runs:
  * rows [s * shard_rows, (s + 1) * shard_rows) of op(A) may be read once
  * ready[s] has reached `epoch` (wrap-safe), batch entry b of op(B) once

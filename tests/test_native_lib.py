@@ -109,6 +109,24 @@ def test_noalloc_argument_checks_without_gpu():
     assert fn(4096, 4096, 4096, 1.0, FAKE, 4096, 0, FAKE, 4096, 0, 0.0, None, 0, FAKE, 4096, None) == N.ERR_WORKSPACE
 
 
+def test_symm_argument_checks_without_gpu():
+    """trnblas_symm takes the kernel dtypes, and a leading dimension of the
+    symmetric operand below n is refused before any device work; the 16-bit
+    form needs the full symmetric operand's bytes of workspace."""
+    fn = N.lib().trnblas_symm
+    assert fn(99, 0, 1, 64, 32, 1.0, FAKE, 64, FAKE, 32, 0.0, None, 0, FAKE, 32, None, 0, None) == N.ERR_ARG
+    assert "dtype" in N.last_error()
+    assert fn(N.BF16, 0, 1, 64, 32, 1.0, FAKE, 32, FAKE, 32, 0.0, None, 0, FAKE, 32, None, 0, None) == N.ERR_ARG
+    assert fn(N.BF16, 0, 1, 64, 32, 1.0, FAKE, 64, FAKE, 32, 0.0, None, 0, FAKE, 32, None, 0, None) == N.ERR_WORKSPACE
+    assert N.lib().trnblas_symm_workspace_size(N.BF16, 0, 100, 7) >= 100 * 104 * 2
+    assert N.lib().trnblas_symm_workspace_size(N.F32, 1, 7, 100) == N.lib().trnblas_gemm_workspace_size(N.F32, 1, 7, 100, 100, 0, 0)
+    # side left: S is op(A) (64 x 64), lda 32 < 64
+    assert fn(N.F32, 0, 1, 64, 32, 1.0, FAKE, 32, FAKE, 32, 0.0, None, 0, FAKE, 32, None, 0, None) == N.ERR_ARG
+    # side right: S is op(B) (32 x 32), lda 16 < 32
+    assert fn(N.F32, 1, 0, 64, 32, 1.0, FAKE, 16, FAKE, 32, 0.0, None, 0, FAKE, 32, None, 0, None) == N.ERR_ARG
+    assert "lda/ldb" in N.last_error()
+
+
 def test_dtype_codes():
     import torch
 

@@ -85,3 +85,38 @@ def test_trmm_triangle_blocks_every_case(dt, tol, n, m):
                 ref = 0.5 * (T @ X.double() if side == "left" else X.double() @ T)
                 assert R.dtype == dt
                 assert blas3.relf(R.double().cpu().numpy(), ref.cpu().numpy()) <= tol, (side, uplo, trans)
+
+
+@pytest.mark.parametrize("dt,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
+@pytest.mark.parametrize("n,m", [(300, 130), (2600, 1900)])
+def test_symm_reads_only_the_triangle(dt, tol, n, m):
+    """symm runs trnblas_symm: the fp32 split pass (or the 16-bit fill pass)
+    reads the symmetric operand from its stored triangle (the other one holds
+    NaN here and is never read). Both sides and triangles, a column-major A
+    (its stored triangle is the other one of the memory), a strided B and a
+    broadcasting C, at a one-CTA size and at a CTA-pair size (2600 x 1900:
+    88 pair tiles), against fp64."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    S = torch.randn(n, n, device="cuda", generator=g, dtype=torch.float64)
+    S = S + S.T
+    for side in ("left", "right"):
+        X = torch.randn(*((n, m) if side == "left" else (m, n)), device="cuda", generator=g).to(dt)
+        ref_core = (S @ X.double()) if side == "left" else (X.double() @ S)
+        for uplo in ("lower", "upper"):
+            keep = torch.ones(n, n, dtype=torch.bool, device="cuda")
+            keep = keep.tril() if uplo == "lower" else keep.triu()
+            A = torch.where(keep, S, torch.full_like(S, float("nan"))).to(dt)
+            R = tb.symm(0.5, A, X, 2.0, ref_core.to(dt), side=side, uplo=uplo)
+            assert R.dtype == dt
+            assert blas3.relf(R.double().cpu().numpy(), (2.5 * ref_core).cpu().numpy()) <= tol, (side, uplo)
+            # column-major storage of the same logical A
+            Acm = A.T.contiguous().T
+            R2 = tb.symm(1.0, Acm, X, side=side, uplo=uplo)
+            assert blas3.relf(R2.double().cpu().numpy(), ref_core.cpu().numpy()) <= tol, (side, uplo, "cm")
+    # strided B (every other column of a wider tensor) and a row-vector C
+    Xw = torch.randn(n, 2 * m, device="cuda", generator=g).to(dt)[:, ::2]
+    Crow = torch.randn(1, m, device="cuda", generator=g).to(dt)
+    S16 = S.to(dt)
+    R3 = tb.symm(1.0, S16, Xw, 0.25, Crow, side="left", uplo="lower")
+    ref3 = S16.double() @ Xw.double() + 0.25 * Crow.double()
+    assert blas3.relf(R3.double().cpu().numpy(), ref3.cpu().numpy()) <= tol

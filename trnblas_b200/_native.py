@@ -42,6 +42,10 @@ _SIGNATURES = {
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,
          _i64, _p, _i64, _i64, _i, _p, _sz, _p],
     ),
+    "trnblas_symm_workspace_size": (_sz, [_i, _i, _i64, _i64]),
+    "trnblas_symm": (
+        _i, [_i, _i, _i, _i64, _i64, _f, _p, _i64, _p, _i64, _f, _p, _i64, _p, _i64, _p, _sz, _p]
+    ),
     "trnblas_gemm_ready": (
         _i,
         [_i, _i64, _i64, _i64, _i64, _f, _p, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _p, _i64,

@@ -367,6 +367,98 @@ int launch_split(const float* X, long long rs, long long ks, long long bs, long 
   return TRNBLAS_OK;
 }
 
+// The split of a symmetric n x n operand S read from its stored triangle
+// (row-major, leading dimension lds; `lower`: S[r][k] = A[r][k] for r >= k,
+// else A[k][r]), into K-major planes hi / lo of n rows by kp = round_up(n, 4)
+// (the symm path: no materialised full S). 32 x 32 tiles: a tile below the
+// stored diagonal is read in place (lanes along k), one above it through the
+// transpose (lanes along r, the tile of the mirrored block), a diagonal tile
+// both ways, each element taking the one from the stored triangle.
+__global__ void split_tf32_sym_kernel(const float* __restrict__ X, long long lds, int n, int lower,
+                                      int kp, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float direct[32][33], mirror[32][33];
+  const int k0 = blockIdx.x * 32;
+  const int r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  // in the stored triangle: r >= k (lower) or r <= k (upper)
+  const bool all_stored = lower ? (r0 >= k0 + 31) : (r0 + 31 <= k0);
+  const bool none_stored = lower ? (r0 + 31 < k0) : (r0 > k0 + 31);
+  if (!none_stored) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      direct[i][tx] = (r < n && k < n) ? __ldg(X + static_cast<long long>(r) * lds + k) : 0.0f;
+    }
+  }
+  if (!all_stored) {
+    // S[r][k] = A[k][r]: read rows k of A along r, store transposed
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      mirror[tx][i] = (r < n && k < n) ? __ldg(X + static_cast<long long>(k) * lds + r) : 0.0f;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, k = k0 + tx;
+    if (r < n && k < kp) {
+      const bool stored = lower ? (r >= k) : (r <= k);
+      const float x = (k < n) ? (stored ? direct[i][tx] : mirror[i][tx]) : 0.0f;
+      float h, l;
+      split1(x, h, l);
+      const long long o = static_cast<long long>(r) * kp + k;
+      hi[o] = h;
+      lo[o] = l;
+    }
+  }
+}
+
+// The full symmetric n x n matrix of 16-bit elements (bf16 / fp16 bit
+// patterns copied as they are) from the stored triangle of X, into S
+// (row-major, leading dimension ldo >= n): the same tile scheme as
+// split_tf32_sym_kernel, one pass.
+__global__ void sym_fill16_kernel(const uint16_t* __restrict__ X, long long lds, int n, int lower,
+                                  long long ldo, uint16_t* __restrict__ S) {
+  __shared__ uint16_t direct[32][33], mirror[32][33];
+  const int k0 = blockIdx.x * 32;
+  const int r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const bool all_stored = lower ? (r0 >= k0 + 31) : (r0 + 31 <= k0);
+  const bool none_stored = lower ? (r0 + 31 < k0) : (r0 > k0 + 31);
+  if (!none_stored) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      direct[i][tx] = (r < n && k < n) ? X[static_cast<long long>(r) * lds + k] : uint16_t(0);
+    }
+  }
+  if (!all_stored) {
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      mirror[tx][i] = (r < n && k < n) ? X[static_cast<long long>(k) * lds + r] : uint16_t(0);
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, k = k0 + tx;
+    if (r < n && k < n) {
+      const bool stored = lower ? (r >= k) : (r <= k);
+      S[static_cast<long long>(r) * ldo + k] = stored ? direct[i][tx] : mirror[i][tx];
+    }
+  }
+}
+
+int launch_split_sym(const float* X, long long lds, long long n, int lower, float* hi, float* lo,
+                     cudaStream_t stream) {
+  const long long kp = round_up(std::max<long long>(n, 1), 4);
+  dim3 grid(static_cast<unsigned>(ceil_div(kp, 32)), static_cast<unsigned>(ceil_div(n, 32)), 1);
+  if (grid.y > 65535) {
+    set_error("symmetric split grid too large");
+    return TRNBLAS_ERR_ARG;
+  }
+  split_tf32_sym_kernel<<<grid, dim3(32, 8), 0, stream>>>(X, lds, static_cast<int>(n), lower,
+                                                          static_cast<int>(kp), hi, lo);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "symmetric split kernel launch");
+}
+
 // Pick BN for the bf16/fp16 GEMM: 256 unless 128 balances the waves better.
 int pick_bn(long long batch, long long M, long long N) {
   if (N <= 128) return 128;
@@ -410,7 +502,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
                      int64_t ldb, int64_t strideB, int transB, float beta, const void* C,
                      int64_t ldc, int64_t strideC, void* D, int64_t ldd, int64_t strideD,
                      void* workspace, size_t workspace_bytes, void* stream_, const ReadySpec* rs,
-                     int tri = 0) {
+                     int tri = 0, int sym = 0) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (int rc = check_dims(batch, M, N, K)) return rc;
   if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
@@ -500,7 +592,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   auto tma_f32 = [](const void* X, long long ld, long long bstride, bool batched) {
     return (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ld % 4 == 0 && (!batched || bstride % 4 == 0);
   };
-  if (dtype == TRNBLAS_F32 && use_fused_tf32() && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
+  if (dtype == TRNBLAS_F32 && !sym && use_fused_tf32() && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
       tma_f32(B, ldb, strideB, b_b)) {
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     p.a_mn = transA ? 1 : 0;
@@ -536,8 +628,16 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     // op(A)(m, k) and op(B)^T(n, k) strides
     const long long ars = transA ? 1 : lda, aks = transA ? lda : 1;
     const long long brs = transB ? ldb : 1, bks = transB ? 1 : ldb;
-    if (int rc = launch_split(Af, ars, aks, a_b ? strideA : 0, nba, M, K, ahi, alo, stream)) return rc;
-    if (int rc = launch_split(Bf, brs, bks, b_b ? strideB : 0, nbb, N, K, bhi, blo, stream)) return rc;
+    // sym: op(A) (1 / 2) or op(B) (3 / 4) is symmetric, read from its stored
+    // lower (1 / 3) or upper (2 / 4) triangle by the symmetric split
+    if (int rc = (sym == 1 || sym == 2)
+                     ? launch_split_sym(Af, lda, M, sym == 1, ahi, alo, stream)
+                     : launch_split(Af, ars, aks, a_b ? strideA : 0, nba, M, K, ahi, alo, stream))
+      return rc;
+    if (int rc = (sym == 3 || sym == 4)
+                     ? launch_split_sym(Bf, ldb, N, sym == 3, bhi, blo, stream)
+                     : launch_split(Bf, brs, bks, b_b ? strideB : 0, nbb, N, K, bhi, blo, stream))
+      return rc;
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     if (!encode_map_3d(&ma0, dt, 4, ahi, K, M, nba, kp, M * kp, 32, 128) ||
         !encode_map_3d(&ma1, dt, 4, alo, K, M, nba, kp, M * kp, 32, 128) ||
@@ -628,6 +728,66 @@ int trnblas_gemm_tri(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   return gemm_impl(dtype, batch, M, N, K, alpha, A, lda, strideA, transA, B, ldb, strideB, transB,
                    beta, C, ldc, strideC, D, ldd, strideD, workspace, workspace_bytes, stream,
                    nullptr, tri);
+}
+
+size_t trnblas_symm_workspace_size(int dtype, int side_right, int64_t M, int64_t N) {
+  const int64_t n = side_right ? N : M;
+  if (dtype == TRNBLAS_F32) return trnblas_gemm_workspace_size(dtype, 1, M, N, n, 0, 0);
+  if (n <= 0) return 256;
+  // the full symmetric operand, rows padded to 8 elements (16 bytes)
+  return static_cast<size_t>(round_up(n * round_up(n, 8) * 2, 256));
+}
+
+int trnblas_symm(int dtype, int side_right, int uplo_lower, int64_t M, int64_t N, float alpha,
+                 const void* A, int64_t lda, const void* B, int64_t ldb, float beta, const void* C,
+                 int64_t ldc, void* D, int64_t ldd, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (dtype != TRNBLAS_F32 && !valid_dtype_f16(dtype)) {
+    set_error("trnblas_symm: dtype must be F32, BF16 or F16");
+    return TRNBLAS_ERR_ARG;
+  }
+  if (valid_dtype_f16(dtype)) {
+    // 16-bit: the full symmetric operand formed in the workspace in one pass
+    // from the stored triangle, then the GEMM kernel on it
+    const long long n = side_right ? N : M;
+    if (int rc = check_dims(1, M, N, n)) return rc;
+    if (M == 0 || N == 0) return TRNBLAS_OK;
+    if (n > 0 && (!A || lda < n)) {
+      set_error("trnblas_symm: lda/ldb smaller than the stored row length (or NULL A)");
+      return TRNBLAS_ERR_ARG;
+    }
+    const long long lds = round_up(std::max<long long>(n, 1), 8);
+    const size_t need = trnblas_symm_workspace_size(dtype, side_right, M, N);
+    if (n > 0) {
+      if (!workspace || workspace_bytes < need) {
+        set_error("trnblas_symm: 16-bit needs " + std::to_string(need) + " workspace bytes");
+        return TRNBLAS_ERR_WORKSPACE;
+      }
+      if (ceil_div(n, 32) > 65535) {
+        set_error("trnblas_symm: n too large for the fill grid");
+        return TRNBLAS_ERR_ARG;
+      }
+      const dim3 grid(static_cast<unsigned>(ceil_div(n, 32)), static_cast<unsigned>(ceil_div(n, 32)), 1);
+      sym_fill16_kernel<<<grid, dim3(32, 8), 0, static_cast<cudaStream_t>(stream)>>>(
+          static_cast<const uint16_t*>(A), lda, static_cast<int>(n), uplo_lower, lds,
+          static_cast<uint16_t*>(workspace));
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "symmetric fill kernel launch");
+    }
+    if (!side_right)
+      return gemm_impl(dtype, 1, M, N, n, alpha, workspace, lds, 0, 0, B, ldb, 0, 0, beta, C, ldc, 0,
+                       D, ldd, 0, nullptr, 0, stream, nullptr);
+    return gemm_impl(dtype, 1, M, N, n, alpha, B, ldb, 0, 0, workspace, lds, 0, 0, beta, C, ldc, 0, D,
+                     ldd, 0, nullptr, 0, stream, nullptr);
+  }
+  if (!side_right) {
+    // D = alpha S B + beta C: S (M x M) is op(A), read from its stored triangle
+    return gemm_impl(dtype, 1, M, N, M, alpha, A, lda, 0, 0, B, ldb, 0, 0, beta, C, ldc, 0, D, ldd,
+                     0, workspace, workspace_bytes, stream, nullptr, 0, uplo_lower ? 1 : 2);
+  }
+  // D = alpha B S + beta C: S (N x N) is op(B)
+  return gemm_impl(dtype, 1, M, N, N, alpha, B, ldb, 0, 0, A, lda, 0, 0, beta, C, ldc, 0, D, ldd, 0,
+                   workspace, workspace_bytes, stream, nullptr, 0, uplo_lower ? 3 : 4);
 }
 
 int trnblas_gemm_ready(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,

@@ -757,15 +757,21 @@ def symm(
 ) -> torch.Tensor:
     """Symmetric matrix multiply (trnblas/level3.py:196-240):
     C = alpha * A @ B + beta * C (side 'left') or alpha * B @ A + beta * C
-    ('right'), A symmetric with only its `uplo` triangle read. The full
-    symmetric operand is formed on the operands' device (one elementwise
-    pass over n x n), then one GEMM on the tcgen05 kernel with alpha, beta and
-    C fused in its epilogue (same C rules as `gemm`)."""
+    ('right'), A symmetric with only its `uplo` triangle read.
+
+    Kernel dtypes with a 2-D B run `trnblas_symm`: for fp32 the 3xTF32 split
+    pass reads the symmetric operand from the stored triangle (no full matrix
+    is formed), for bf16 / fp16 one pass writes the full matrix from the
+    triangle into the workspace; then the GEMM kernel with alpha, beta and C
+    fused (same C rules as `gemm`)."""
     side, uplo = side_flag(side), uplo_flag(uplo)
     if A.dim() != 2 or A.shape[0] != A.shape[1]:
         raise ValueError(f"symm: A must be a square matrix, got {tuple(A.shape)}")
     if A.dtype in N.KERNEL_DTYPES and B.dtype == A.dtype:
         dev = _cuda_device(A, B, C)
+        if B.dim() == 2:
+            r = _symm_kernel(alpha, _to(A, dev), _to(B, dev), beta, _to(C, dev), side, uplo)
+            return _home(r, A.device, dev)
         S = _sym_full(_to(A, dev), uplo)
         if A.device != dev:
             r = gemm(alpha, S, _to(B, dev), beta, _to(C, dev)) if side == "left" else gemm(alpha, _to(B, dev), S, beta, _to(C, dev))
@@ -773,6 +779,53 @@ def symm(
     else:
         S = _sym_full(A, uplo)
     return gemm(alpha, S, B, beta, C) if side == "left" else gemm(alpha, B, S, beta, C)
+
+
+def _symm_kernel(alpha, a, b, beta, Cd, side, uplo):
+    """symm on the device through trnblas_symm (the symmetric operand read
+    from its stored triangle)."""
+    n = a.shape[0]
+    if side == "left" and b.shape[0] != n or side == "right" and b.shape[1] != n:
+        lhs, rhs = (a.shape, b.shape) if side == "left" else (b.shape, a.shape)
+        raise RuntimeError(f"mat1 and mat2 shapes cannot be multiplied ({lhs[0]}x{lhs[1]} and {rhs[0]}x{rhs[1]})")
+    if a.stride(1) != 1:
+        if a.stride(0) == 1:
+            # a column-major A is the row-major storage of A^T = A, whose
+            # stored triangle is the other one
+            a, uplo = a.mT, ("lower" if uplo == "upper" else "upper")
+        else:
+            a = a.contiguous()
+    lda = max(a.stride(0), n, 1)
+    M, Nn = b.shape
+    dev = b.device
+    dt = a.dtype
+    code = N.dtype_code(dt)
+    if code == N.F32:
+        x = b if b.stride(1) == 1 and b.stride(0) >= Nn else b.contiguous()
+        ldx = max(x.stride(0), Nn, 1)
+    else:
+        # 16-bit B goes to the GEMM kernel's TMA as it lies: row-major, 16-byte
+        # rows and base (else a padded copy)
+        x, ldx, tr = _tma_operand(b, b.element_size())
+        if tr:
+            x, ldx, _ = _tma_operand(b.contiguous(), b.element_size())
+    out = torch.empty((M, Nn), dtype=dt, device=dev)
+    if M == 0 or Nn == 0:
+        return out
+    fuse = _fuse_c(Cd, beta, (M, Nn), dt, dev)
+    c_arg, ldc = None, 0
+    if fuse:
+        c_arg = Cd if Cd.stride(1) == 1 and Cd.stride(0) >= Nn else Cd.contiguous()
+        ldc = c_arg.stride(0)
+    ws_bytes = N.lib().trnblas_symm_workspace_size(code, int(side == "right"), M, Nn)
+    ws = N.workspace(ws_bytes, dev)
+    rc = N.lib().trnblas_symm(code, int(side == "right"), int(uplo == "lower"), M, Nn, float(alpha),
+                              N.ptr(a), lda, N.ptr(x), ldx,
+                              float(beta) if fuse else 0.0, N.ptr(c_arg), ldc, N.ptr(out), Nn,
+                              N.ptr(ws), ws_bytes, N.stream_ptr(dev))
+    N.check(rc, "trnblas_symm")
+    N.count_launches(3 if code == N.F32 else 2)  # symmetric split / fill, (split of B,) GEMM
+    return out if fuse else _add_c(out, beta, Cd)
 
 
 def trmm(

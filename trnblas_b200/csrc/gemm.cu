@@ -152,6 +152,26 @@ __global__ void split_tf32_t64_kernel(const float* __restrict__ X, long long ks,
   }
 }
 
+// The strictly upper triangle of an fp32 n x n matrix from its lower
+// triangle, D[c][r] = D[r][c] for r > c (the CTA-pair SYRK writes whole lower
+// pair tiles, diagonal tiles included): 32 x 32 tiles below or on the
+// diagonal, each read row-wise and written transposed through shared memory.
+__global__ void syrk_mirror_kernel(float* __restrict__ D, long long ldd, int n) {
+  __shared__ float t[32][33];
+  const int bx = blockIdx.x, by = blockIdx.y;  // source tile: row block by, column block bx
+  if (by < bx) return;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int i = ty; i < 32; i += 8) {
+    const int r = by * 32 + i, c = bx * 32 + tx;
+    t[i][tx] = (r < n && c < n) ? D[static_cast<long long>(r) * ldd + c] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int rr = bx * 32 + i, cc = by * 32 + tx;  // destination (rr, cc) = source (cc, rr)
+    if (rr < n && cc < n && cc > rr) D[static_cast<long long>(rr) * ldd + cc] = t[tx][i];
+  }
+}
+
 // D = beta * C (K == 0): an empty sum times alpha is zero.
 __global__ void scale_c_kernel(int out_kind, long long batch, int M, int N, float beta,
                                const void* C, long long ldc, long long strideC, void* D,
@@ -889,6 +909,20 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
         !encode_map_3d(&ma1, dt, 4, alo, k, n, 1, kp, n * kp, 32, 128))
       return TRNBLAS_ERR_ALIGN;
     p.in_fmt = kFmtTF32;
+    const long long T = ceil_div(n, 256);
+    if (use_pair_gemm(1, n, n) && T * (T + 1) / 2 >= num_sms() / 2 && p.c_mode != kCTrans) {
+      // CTA pairs over the lower triangle's 256 x 256 tiles (the 3xTF32 MMAs
+      // of a 128 x 128 tile are shared-memory bound); the pair epilogue
+      // writes whole tiles (C read in place, lower storage), then the strictly
+      // upper triangle is mirrored from the lower one in a second pass
+      p.tiles_m = p.tiles_n = static_cast<int>(T);
+      p.num_tiles = static_cast<int>(T * (T + 1) / 2);
+      if (int rc = launch_gemm_pair<kTF32x3, 3>(ma0, ma1, ma0, ma1, p, stream)) return rc;
+      const dim3 grid(static_cast<unsigned>(ceil_div(n, 32)), static_cast<unsigned>(ceil_div(n, 32)), 1);
+      syrk_mirror_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<float*>(D), ldd, static_cast<int>(n));
+      cudaError_t e = cudaGetLastError();
+      return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "syrk mirror kernel launch");
+    }
     return launch_gemm<kTF32x3, 128, 3>(ma0, ma1, ma0, ma1, p, stream);
   }
   const auto dt = map_dtype(dtype);

@@ -76,7 +76,7 @@ def pair_range_energy(
         N.ptr(out), N.ptr(ws), ws_bytes, N.stream_ptr(dev),
     )
     N.check(rc, "trnblas_pair_energy")
-    N.count_launches(6)  # 4 split kernels, the fused energy kernel, the final sum
+    N.count_launches(7)  # 4 split kernels, the pair order, the fused energy kernel, the final sum
     return out
 
 

@@ -152,18 +152,21 @@ __global__ void split_tf32_t64_kernel(const float* __restrict__ X, long long ks,
   }
 }
 
-// The strictly upper triangle of an fp32 n x n matrix from its lower
-// triangle, D[c][r] = D[r][c] for r > c (the CTA-pair SYRK writes whole lower
-// pair tiles, diagonal tiles included): 32 x 32 tiles below or on the
-// diagonal, each read row-wise and written transposed through shared memory.
-__global__ void syrk_mirror_kernel(float* __restrict__ D, long long ldd, int n) {
-  __shared__ float t[32][33];
+// The strictly upper triangle of an n x n matrix from its lower triangle,
+// D[c][r] = D[r][c] for r > c (the CTA-pair SYRK writes whole lower pair
+// tiles, diagonal tiles included): 32 x 32 tiles below or on the diagonal,
+// each read row-wise and written transposed through shared memory. (Also
+// tried for bf16 with uint16_t bit patterns: 861 against 934 TFLOP/s for the
+// one-CTA column-block-pair kernel at n = k = 4096, so 16-bit SYRK keeps that.)
+template <typename T>
+__global__ void syrk_mirror_kernel(T* __restrict__ D, long long ldd, int n) {
+  __shared__ T t[32][33];
   const int bx = blockIdx.x, by = blockIdx.y;  // source tile: row block by, column block bx
   if (by < bx) return;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
   for (int i = ty; i < 32; i += 8) {
     const int r = by * 32 + i, c = bx * 32 + tx;
-    t[i][tx] = (r < n && c < n) ? D[static_cast<long long>(r) * ldd + c] : 0.0f;
+    t[i][tx] = (r < n && c < n) ? D[static_cast<long long>(r) * ldd + c] : T(0);
   }
   __syncthreads();
   for (int i = ty; i < 32; i += 8) {
@@ -919,7 +922,7 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
       p.num_tiles = static_cast<int>(T * (T + 1) / 2);
       if (int rc = launch_gemm_pair<kTF32x3, 3>(ma0, ma1, ma0, ma1, p, stream)) return rc;
       const dim3 grid(static_cast<unsigned>(ceil_div(n, 32)), static_cast<unsigned>(ceil_div(n, 32)), 1);
-      syrk_mirror_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<float*>(D), ldd, static_cast<int>(n));
+      syrk_mirror_kernel<float><<<grid, dim3(32, 8), 0, stream>>>(static_cast<float*>(D), ldd, static_cast<int>(n));
       cudaError_t e = cudaGetLastError();
       return e == cudaSuccess ? TRNBLAS_OK : cuda_fail(e, "syrk mirror kernel launch");
     }

@@ -454,16 +454,15 @@ def _syrk_kernel(a_eff: torch.Tensor, alpha: float, beta: float, C, c_uplo: int)
         N.ptr(out), n, N.ptr(ws), ws_bytes, N.stream_ptr(dev),
     )
     N.check(rc, "trnblas_syrk")
-    if code == N.F32:
-        # split + GEMM, and the mirror pass when the CTA-pair kernel ran (a
-        # full wave of lower-triangle pair tiles, C absent or lower-stored)
-        T = -(-n // 256)
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        pair = (T * (T + 1) // 2 >= sms // 2 and n > 128 and not (c_arg is not None and c_uplo == 2)
-                and os.environ.get("TRNBLAS_B200_GEMM_PAIR", "1") != "0")
-        N.count_launches(3 if pair else 2)
-    else:
-        N.count_launches(1)
+    # (the fp32 split +) the GEMM, and for fp32 the mirror pass when the
+    # CTA-pair kernel ran (a full wave of lower-triangle pair tiles, C absent
+    # or lower-stored)
+    T = -(-n // 256)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    pair = (code == N.F32 and T * (T + 1) // 2 >= sms // 2 and n > 128
+            and not (c_arg is not None and c_uplo == 2)
+            and os.environ.get("TRNBLAS_B200_GEMM_PAIR", "1") != "0")
+    N.count_launches((2 if code == N.F32 else 1) + (1 if pair else 0))
     return out
 
 

@@ -256,11 +256,11 @@ TRAFFIC = {
     "gemm8192_fp32": 4821362688,   # profiles/gemm_fp32_8192.md
     "batched": 313154560,          # profiles/gemm_batched_64x512.md
     "batched_bf16": 70896640,      # profiles/gemm_batched_bf16.md
-    "syrk": 528911104,             # profiles/gemm_syrk_4096.md
+    "syrk": 257120256,             # profiles/gemm_syrk_4096.md
     "syrk_bf16": 34854912,         # profiles/gemm_syrk_bf16_4096.md
     "gemm_fp64": 2161969960,       # profiles/ozaki_fp64_4096.md (the int8 GEMM kernel)
-    "pair3": 376285440,            # profiles/pair_energy_pair3.md
-    "pair5x4": 2798001576,         # profiles/pair_energy_pair5x4.md
+    "pair3": 350738688,            # profiles/pair_energy_pair3.md
+    "pair5x4": 2716847520,         # profiles/pair_energy_pair5x4.md
     "pair5": 1643160000000,        # profiles/pair_energy_pair5_dram.md
 }
 

@@ -617,17 +617,15 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   };
   if (dtype == TRNBLAS_F32 && !sym && use_fused_tf32() && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
       tma_f32(B, ldb, strideB, b_b)) {
+    // both operands K-major here (op(A) stored M x K, op(B) stored N x K)
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    p.a_mn = transA ? 1 : 0;
-    p.b_mn = transB ? 0 : 1;
+    p.a_mn = 0;
+    p.b_mn = 0;
     p.in_fmt = kFmtTF32;
-    const long long a_rows = transA ? K : M, b_rows = transB ? N : K;
-    const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 4);
-    const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 4);
-    bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 4, A, M, K, nba, lda, sa2, 32, 32)
-                     : encode_map_3d(&ma0, dt, 4, A, K, M, nba, lda, sa2, 32, 128);
-    ok = ok && (p.b_mn ? encode_map_3d(&mb0, dt, 4, B, N, K, nbb, ldb, sb2, 32, 32)
-                       : encode_map_3d(&mb0, dt, 4, B, K, N, nbb, ldb, sb2, 32, 128));
+    const long long sa2 = a_b ? strideA : round_up(lda * M, 4);
+    const long long sb2 = b_b ? strideB : round_up(ldb * N, 4);
+    const bool ok = encode_map_3d(&ma0, dt, 4, A, K, M, nba, lda, sa2, 32, 128) &&
+                    encode_map_3d(&mb0, dt, 4, B, K, N, nbb, ldb, sb2, 32, 128);
     if (!ok) return TRNBLAS_ERR_ALIGN;
     p.tiles_m = static_cast<int>(ceil_div(M, 128));
     p.tiles_n = static_cast<int>(ceil_div(N, 128));
@@ -884,14 +882,13 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
   CUtensorMap ma0, ma1;
   if (dtype == TRNBLAS_F32 && use_fused_tf32() && !trans && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
       lda % 4 == 0) {
-    // the split fused into the kernel: raw fp32 tiles of A for both operands
+    // the split fused into the kernel: raw fp32 K-major tiles of A for both
+    // operands
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    p.a_mn = p.b_mn = trans ? 1 : 0;
+    p.a_mn = p.b_mn = 0;
     p.in_fmt = kFmtTF32;
-    const long long s2 = round_up(lda * (trans ? k : n), 4);
-    const bool ok = trans ? encode_map_3d(&ma0, dt, 4, A, n, k, 1, lda, s2, 32, 32)
-                          : encode_map_3d(&ma0, dt, 4, A, k, n, 1, lda, s2, 32, 128);
-    if (!ok) return TRNBLAS_ERR_ALIGN;
+    if (!encode_map_3d(&ma0, dt, 4, A, k, n, 1, lda, round_up(lda * n, 4), 32, 128))
+      return TRNBLAS_ERR_ALIGN;
     return launch_gemm<kTF32x3F, 128, 3>(ma0, ma0, ma0, ma0, p, stream);
   }
   if (dtype == TRNBLAS_F32) {

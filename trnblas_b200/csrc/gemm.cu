@@ -773,8 +773,10 @@ int trnblas_symm(int dtype, int side_right, int uplo_lower, int64_t M, int64_t N
     const long long n = side_right ? N : M;
     if (int rc = check_dims(1, M, N, n)) return rc;
     if (M == 0 || N == 0) return TRNBLAS_OK;
-    if (n > 0 && (!A || lda < n)) {
-      set_error("trnblas_symm: lda/ldb smaller than the stored row length (or NULL A)");
+    // every argument the GEMM will check, before the fill pass is queued
+    if (!D || ldd < N || (C && beta != 0.0f && ldc < N) ||
+        (n > 0 && (!A || !B || lda < n || ldb < N))) {
+      set_error("trnblas_symm: NULL operand, or lda/ldb/ldc/ldd smaller than the stored row length");
       return TRNBLAS_ERR_ARG;
     }
     const long long lds = round_up(std::max<long long>(n, 1), 8);

@@ -30,10 +30,10 @@ def _status_clean():
     assert tb.device_status(0) == 0, "a kernel gave up a bounded wait"
 
 
-# The last: 81 CTA-pair tiles (at least one per SM pair: the pair kernel)
-# with ragged edges; the others run on the one-CTA kernel.
+# The last: 81 CTA-pair tiles (at least one per SM pair) and K >= 1024, the
+# pair kernel, with ragged edges; the others run on the one-CTA kernel.
 SHAPES = [(128, 128, 64), (256, 512, 128), (127, 129, 65), (300, 200, 17), (1, 1, 1), (640, 384, 1000), (1000, 33, 257),
-          (130, 520, 96), (1500, 700, 333), (2300, 2100, 333)]
+          (130, 520, 96), (1500, 700, 333), (2300, 2100, 1100)]
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
@@ -126,6 +126,19 @@ def test_batched_config2(dt):
     assert relf(out, A.double() @ B.double()) <= TOL[dt]
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_batched_on_cta_pairs(dt):
+    """20 x (512 x 520 x 1100), transposed B, fused C: 20 x 2 x 3 pair tiles
+    with K >= 1024 run the CTA-pair kernel with the batch in its tile walk."""
+    g = torch.Generator(device=DEV).manual_seed(21)
+    A = torch.randn(20, 512, 1100, device=DEV, generator=g).to(dt)
+    Bt = torch.randn(20, 520, 1100, device=DEV, generator=g).to(dt)
+    C = torch.randn(20, 512, 520, device=DEV, generator=g).to(dt)
+    out = tb.batched_gemm(0.5, A, Bt, 2.0, C, transB=True)
+    ref = 0.5 * A.double() @ Bt.double().transpose(1, 2) + 2.0 * C.double()
+    assert out.dtype == dt and relf(out, ref) <= TOL[dt]
+
+
 def test_batched_broadcast_trans_and_c():
     g = np.load("tests/golden/gemm.npz")
     A, B, B2, C = (torch.from_numpy(g[f"b0_{k}"]).to(DEV) for k in ("A", "B", "B2", "C"))
@@ -138,9 +151,9 @@ def test_batched_broadcast_trans_and_c():
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
-# (3000, 300): 78 lower-triangle 256 x 256 tiles, the fp32 CTA-pair kernel
-# plus the mirror pass (upper-stored C keeps the one-CTA kernel)
-@pytest.mark.parametrize("n,k", [(128, 64), (300, 200), (1000, 512), (129, 1), (3000, 300)])
+# (3000, 1100): 78 lower-triangle 256 x 256 tiles and k >= 1024, the fp32
+# CTA-pair kernel plus the mirror pass (upper-stored C keeps the one-CTA kernel)
+@pytest.mark.parametrize("n,k", [(128, 64), (300, 200), (1000, 512), (129, 1), (3000, 1100)])
 @pytest.mark.parametrize("trans", [False, True])
 @pytest.mark.parametrize("uplo", ["lower", "upper"])
 def test_syrk_exactly_symmetric(dt, n, k, trans, uplo):

@@ -297,21 +297,23 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& a1, const CUtensor
 bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBLAS_F16; }
 
 // CTA-pair tiles (256 x 256) when there are at least as many pair tiles as
-// SM pairs (one full wave) and M, N > 128; smaller problems keep the one-CTA
-// kernel, whose smaller tiles occupy more SMs (fp32 1024^3: 16 pair tiles on
-// 32 SMs ran at 33 TFLOP/s against 39 for 64 one-CTA tiles).
+// SM pairs (one full wave), M, N > 128 and K >= 1024; smaller problems keep
+// the one-CTA kernel, whose smaller tiles occupy more SMs (fp32 1024^3: 16
+// pair tiles on 32 SMs ran at 33 TFLOP/s against 39 for 64 one-CTA tiles) and
+// whose shorter pipeline fills faster on short K loops (bf16 batched 64 x
+// 512^3: 449 TFLOP/s on pairs against 499 on one-CTA 128 x 256 tiles).
 // TRNBLAS_B200_GEMM_PAIR=0 keeps the one-CTA kernel everywhere.
 // Measured at 32768^3 bf16 under the 1 kW power cap, same box: pair kernel
 // with the wave synchronisation 1347 TFLOP/s (52.6 J a product), one-CTA
 // kernel 1248 TFLOP/s (52.5-58.7 J). Without the wave synchronisation the
 // pair kernel's tiles drift apart and re-read 246 GB from DRAM per product,
 // and it lost (912 against 1130 TFLOP/s).
-bool use_pair_gemm(long long batch, long long M, long long N) {
+bool use_pair_gemm(long long batch, long long M, long long N, long long K) {
   static const int mode = [] {
     const char* s = std::getenv("TRNBLAS_B200_GEMM_PAIR");
     return (s && *s) ? std::atoi(s) : 1;
   }();
-  return mode != 0 && M > 128 && N > 128 &&
+  return mode != 0 && M > 128 && N > 128 && K >= 1024 &&
          batch * ceil_div(M, 256) * ceil_div(N, 256) >= num_sms() / 2;
 }
 
@@ -668,7 +670,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     p.a_mn = 0;
     p.b_mn = 0;
     p.in_fmt = kFmtTF32;
-    if (use_pair_gemm(batch, M, N)) {
+    if (use_pair_gemm(batch, M, N, K)) {
       // 256 x 256 tiles on CTA pairs: each CTA reads half the shared-memory
       // bytes per MMA of a 128 x 128 tile
       p.group_m = group_m_override() ? group_m_override() : 8;
@@ -692,7 +694,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
   const long long b_rows = transB ? N : K;
   const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 8);
   const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 8);
-  if (use_pair_gemm(batch, M, N)) {
+  if (use_pair_gemm(batch, M, N, K)) {
     // 256 x 256 tiles on CTA pairs; each CTA loads 128 rows of A and 128
     // columns of B
     bool ok = p.a_mn ? encode_map_3d(&ma0, dt, 2, A, M, K, nba, lda, sa2, 64, 64)
@@ -912,7 +914,7 @@ int trnblas_syrk(int dtype, int64_t n, int64_t k, float alpha, const void* A, in
       return TRNBLAS_ERR_ALIGN;
     p.in_fmt = kFmtTF32;
     const long long T = ceil_div(n, 256);
-    if (use_pair_gemm(1, n, n) && T * (T + 1) / 2 >= num_sms() / 2 && p.c_mode != kCTrans) {
+    if (use_pair_gemm(1, n, n, k) && T * (T + 1) / 2 >= num_sms() / 2 && p.c_mode != kCTrans) {
       // CTA pairs over the lower triangle's 256 x 256 tiles (the 3xTF32 MMAs
       // of a 128 x 128 tile are shared-memory bound); the pair epilogue
       // writes whole tiles (C read in place, lower storage), then the strictly

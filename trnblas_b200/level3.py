@@ -459,7 +459,7 @@ def _syrk_kernel(a_eff: torch.Tensor, alpha: float, beta: float, C, c_uplo: int)
     # or lower-stored)
     T = -(-n // 256)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    pair = (code == N.F32 and T * (T + 1) // 2 >= sms // 2 and n > 128
+    pair = (code == N.F32 and T * (T + 1) // 2 >= sms // 2 and n > 128 and k >= 1024
             and not (c_arg is not None and c_uplo == 2)
             and os.environ.get("TRNBLAS_B200_GEMM_PAIR", "1") != "0")
     N.count_launches((2 if code == N.F32 else 1) + (1 if pair else 0))

@@ -1,10 +1,10 @@
 """The fp32 GEMM with the 3xTF32 split fused into the kernel, which
-TRNBLAS_B200_TF32_FUSED=1 selects for K-major operands the TMA can read in
-place of the split pass (the default, covered by test_gemm_gpu.py), against
-fp64 products: ragged edges, a long K, a batched call, SYRK and a triangular
-(trmm) product, whose tiles run fewer K blocks than the others. The
-selection is read once per process, so the products run in a child
-process."""
+TRNBLAS_B200_TF32_FUSED=1 selects for operands the TMA can read in place of
+the split pass (the default, covered by test_gemm_gpu.py), against fp64
+products: K-major and MN-major operands (every transpose pair), ragged
+edges, a long K, batched calls, SYRK and a triangular (trmm) product, whose
+tiles run fewer K blocks than the others. The selection is read once per
+process, so the products run in a child process."""
 
 from __future__ import annotations
 
@@ -26,12 +26,23 @@ g = torch.Generator(device="cuda").manual_seed(5)
 out = []
 def relf(x, r):
     return float((x.double() - r).norm() / r.norm())
-for (M, N, K) in [(128, 128, 64), (300, 200, 517), (1500, 700, 333), (1024, 1024, 8192)]:
-    A = torch.randn(M, K, device="cuda", generator=g)
-    Bt = torch.randn(N, K, device="cuda", generator=g)
-    C = torch.randn(M, N, device="cuda", generator=g)
-    r = tb.gemm(0.5, A, Bt, 2.0, C, transB=True)
-    out.append(["gemm", M, N, K, relf(r, 0.5 * A.double() @ Bt.double().T + 2.0 * C.double())])
+for (M, N, K) in [(128, 128, 64), (300, 200, 516), (1500, 700, 332), (1024, 1024, 8192)]:
+    for ta in (False, True):
+        for tbb in (False, True):
+            A = torch.randn(*((K, M) if ta else (M, K)), device="cuda", generator=g)
+            B = torch.randn(*((N, K) if tbb else (K, N)), device="cuda", generator=g)
+            C = torch.randn(M, N, device="cuda", generator=g)
+            r = tb.gemm(0.5, A, B, 2.0, C, transA=ta, transB=tbb)
+            a = A.double().T if ta else A.double()
+            b = B.double().T if tbb else B.double()
+            out.append(["gemm %d%d" % (ta, tbb), M, N, K, relf(r, 0.5 * a @ b + 2.0 * C.double())])
+gen = torch.Generator().manual_seed(0)
+A1, B1, C1 = (2 * torch.rand(1024, 1024, generator=gen) - 1 for _ in range(3))
+r = tb.gemm(1.0, A1.cuda(), B1.cuda(), 0.5, C1.cuda(), transA=True)
+out.append(["config1", 1024, 1024, 1024, relf(r, (A1.double().T @ B1.double() + 0.5 * C1.double()).cuda())])
+A2 = torch.randn(64, 512, 512, device="cuda", generator=g)
+B2 = torch.randn(64, 512, 512, device="cuda", generator=g)
+out.append(["batched 2a", 512, 512, 512, relf(tb.batched_gemm(1.0, A2, B2), A2.double() @ B2.double())])
 A3 = torch.randn(6, 384, 256, device="cuda", generator=g)
 B3 = torch.randn(6, 320, 256, device="cuda", generator=g)
 r = tb.batched_gemm(1.0, A3, B3, transB=True)

@@ -419,6 +419,22 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// MN-major 32-bit (tf32) descriptor: the 128-byte swizzle of 32-byte atoms
+// (UMMA layout type 1, staged by TMA with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B):
+// rows of 128 bytes (32 MN elements) along K, `lbo` between 32-element MN
+// atoms, `sbo` between 4-row K groups (512 for contiguous 128-byte rows).
+// Checked with a standalone MMA against fp64 products before use.
+__device__ __forceinline__ uint64_t sdesc_sw128_atom32(uint32_t saddr, uint32_t lbo_bytes,
+                                                       uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(1) << 61;  // SWIZZLE_128B with 32-byte atoms
+  return d;
+}
+
 // K-major descriptor without swizzle: core matrices of 8 rows x 16 bytes
 // (128 contiguous bytes), the two 16-byte K halves of a 32-byte MMA K step
 // `lbo` apart, consecutive 8-row groups `sbo` apart.

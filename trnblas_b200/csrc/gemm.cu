@@ -609,25 +609,35 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     p.ready_b0 = rs->b0;
     p.rot_b = rs->rot_b;
   }
-  // fp32 with K-major operands the TMA can read (op(A) stored M x K and op(B)
-  // stored N x K, 16-byte aligned bases, row and batch strides multiples of 4
-  // elements), when use_fused_tf32(): the split fused into the GEMM kernel.
-  // (An MN-major tf32 operand needs the 32-byte-atom 128-byte swizzle, which
-  // this kernel does not stage: those operands take the split pass.)
+  // fp32 with operands the TMA can read (16-byte aligned bases, row and batch
+  // strides multiples of 4 elements), when use_fused_tf32(): the split fused
+  // into the GEMM kernel. K-major operands as 128-byte swizzle rows of 32 K,
+  // MN-major ones as boxes of 32 MN x 32 K with the 128-byte swizzle of
+  // 32-byte atoms.
   auto tma_f32 = [](const void* X, long long ld, long long bstride, bool batched) {
     return (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ld % 4 == 0 && (!batched || bstride % 4 == 0);
   };
-  if (dtype == TRNBLAS_F32 && !sym && use_fused_tf32() && !transA && transB && tma_f32(A, lda, strideA, a_b) &&
+  if (dtype == TRNBLAS_F32 && !sym && use_fused_tf32() && tma_f32(A, lda, strideA, a_b) &&
       tma_f32(B, ldb, strideB, b_b)) {
-    // both operands K-major here (op(A) stored M x K, op(B) stored N x K)
     const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    p.a_mn = 0;
-    p.b_mn = 0;
+    p.a_mn = transA ? 1 : 0;  // A stored K x M
+    p.b_mn = transB ? 0 : 1;  // B stored K x N
     p.in_fmt = kFmtTF32;
-    const long long sa2 = a_b ? strideA : round_up(lda * M, 4);
-    const long long sb2 = b_b ? strideB : round_up(ldb * N, 4);
-    const bool ok = encode_map_3d(&ma0, dt, 4, A, K, M, nba, lda, sa2, 32, 128) &&
-                    encode_map_3d(&mb0, dt, 4, B, K, N, nbb, ldb, sb2, 32, 128);
+    const long long a_rows = transA ? K : M, b_rows = transB ? N : K;
+    const long long sa2 = a_b ? strideA : round_up(lda * a_rows, 4);
+    const long long sb2 = b_b ? strideB : round_up(ldb * b_rows, 4);
+    auto mn_map = [&](CUtensorMap* m, const void* X, long long mn, long long ld, long long s2,
+                      long long nb) {
+      const uint64_t dims[3] = {static_cast<uint64_t>(mn), static_cast<uint64_t>(K),
+                                static_cast<uint64_t>(nb)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(ld), static_cast<uint64_t>(s2)};
+      const uint32_t box[3] = {32, 32, 1};
+      return encode_map(m, dt, 4, X, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    };
+    const bool ok = (p.a_mn ? mn_map(&ma0, A, M, lda, sa2, nba)
+                            : encode_map_3d(&ma0, dt, 4, A, K, M, nba, lda, sa2, 32, 128)) &&
+                    (p.b_mn ? mn_map(&mb0, B, N, ldb, sb2, nbb)
+                            : encode_map_3d(&mb0, dt, 4, B, K, N, nbb, ldb, sb2, 32, 128));
     if (!ok) return TRNBLAS_ERR_ALIGN;
     p.tiles_m = static_cast<int>(ceil_div(M, 128));
     p.tiles_n = static_cast<int>(ceil_div(N, 128));

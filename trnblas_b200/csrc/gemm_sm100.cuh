@@ -30,9 +30,9 @@
 namespace tb {
 
 // kTF32x3F: the fp32 API with the split fused into the kernel: TMA loads the
-// raw fp32 tiles (K-major operands only: an MN-major tf32 tile needs the
-// 128-byte swizzle of 32-byte atoms, which this kernel does not stage) into
-// the "hi" slots and converter warps write lo = x - trunc19(x) beside them. The tensor core reads only the top
+// raw fp32 tiles (K-major: 128-byte swizzle rows of 32 K; MN-major: boxes
+// of 32 MN x 32 K with the 128-byte swizzle of 32-byte atoms) into the "hi"
+// slots and converter warps write lo = x - trunc19(x) beside them. The tensor core reads only the top
 // 19 bits of a kind::tf32 operand (measured: a product of raw fp32 inputs
 // equals the product of inputs truncated to tf32 within the fp32 accumulate
 // rounding, 6e-8, and differs from rounded inputs by 1.2e-3), so the raw tile
@@ -214,6 +214,10 @@ __device__ __forceinline__ void gemm_mma_role(const GemmParams& p, uint8_t* smem
     if constexpr (KIND == kF16) {
       ad[kk] = p.a_mn ? sdesc_sw128(sa0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sa0 + kk * 32, 16, 1024);
       bd[kk] = p.b_mn ? sdesc_sw128(sb0 + kk * 2048, 64 * 128, 1024) : sdesc_sw128(sb0 + kk * 32, 16, 1024);
+    } else if constexpr (KIND == kTF32x3F) {
+      // MN-major: 4 KB boxes (32 MN x 32 K rows), one k step = 8 K rows
+      ad[kk] = p.a_mn ? sdesc_sw128_atom32(sa0 + kk * 1024, 32 * 128, 512) : sdesc_sw128(sa0 + kk * 32, 16, 1024);
+      bd[kk] = p.b_mn ? sdesc_sw128_atom32(sb0 + kk * 1024, 32 * 128, 512) : sdesc_sw128(sb0 + kk * 32, 16, 1024);
     } else {
       ad[kk] = sdesc_sw128(sa0 + kk * 32, 16, 1024);
       bd[kk] = sdesc_sw128(sb0 + kk * 32, 16, 1024);
@@ -603,10 +607,21 @@ __global__ void __launch_bounds__(GemmCfg<KIND, BN>::THREADS, 1)
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::LOAD_BYTES);
         const int k0 = kb * BK;
         if (KIND == kTF32x3F) {
-          // raw fp32 tiles into the hi slots (K-major; the host sends no
-          // MN-major operand here)
-          tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
-          tma_load_3d(sb, &map_b0, &full_bar[stage], k0, n0, zb);
+          // raw fp32 tiles into the hi slots (MN-major: boxes of 32 MN x 32 K)
+          if (!p.a_mn) {
+            tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tma_load_3d(sa + j * (32 * 128), &map_a0, &full_bar[stage], m0 + 32 * j, k0, za);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sb, &map_b0, &full_bar[stage], k0, n0, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_3d(sb + j * (32 * 128), &map_b0, &full_bar[stage], n0 + 32 * j, k0, zb);
+          }
         } else if (KIND == kF16) {
           if (!p.a_mn) {
             tma_load_3d(sa, &map_a0, &full_bar[stage], k0, m0, za);

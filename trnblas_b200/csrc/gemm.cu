@@ -308,13 +308,17 @@ bool valid_dtype_f16(int dtype) { return dtype == TRNBLAS_BF16 || dtype == TRNBL
 // kernel 1248 TFLOP/s (52.5-58.7 J). Without the wave synchronisation the
 // pair kernel's tiles drift apart and re-read 246 GB from DRAM per product,
 // and it lost (912 against 1130 TFLOP/s).
-bool use_pair_gemm(long long batch, long long M, long long N, long long K) {
+// `wave_div`: the pair tiles needed, as a fraction 1 / wave_div of the SMs
+// (2: one wave of pairs; fp32 passes 4, since its one-CTA tiles are shared-
+// memory bound and a half-empty wave of pairs still wins: fp32 2048^3, 64
+// pair tiles, 171 against 140 TFLOP/s; 3072^3 231 against 185).
+bool use_pair_gemm(long long batch, long long M, long long N, long long K, int wave_div = 2) {
   static const int mode = [] {
     const char* s = std::getenv("TRNBLAS_B200_GEMM_PAIR");
     return (s && *s) ? std::atoi(s) : 1;
   }();
   return mode != 0 && M > 128 && N > 128 && K >= 1024 &&
-         batch * ceil_div(M, 256) * ceil_div(N, 256) >= num_sms() / 2;
+         batch * ceil_div(M, 256) * ceil_div(N, 256) >= num_sms() / wave_div;
 }
 
 // fp32 (3xTF32) with the split fused into the GEMM kernel (kTF32x3F) instead
@@ -680,7 +684,7 @@ static int gemm_impl(int dtype, int64_t batch, int64_t M, int64_t N, int64_t K, 
     p.a_mn = 0;
     p.b_mn = 0;
     p.in_fmt = kFmtTF32;
-    if (use_pair_gemm(batch, M, N, K)) {
+    if (use_pair_gemm(batch, M, N, K, 4)) {
       // 256 x 256 tiles on CTA pairs: each CTA reads half the shared-memory
       // bytes per MMA of a 128 x 128 tile
       p.group_m = group_m_override() ? group_m_override() : 8;

@@ -461,7 +461,7 @@ def run_gemm_spmd(args, rank, world, gpu, dtype, n=32768):
         c = tp.gemm_2d(a, b, grid, k_chunks=k_chunks)
         Ch.copy_(c, non_blocking=True)
 
-    e2e_ms, _ = timed_steps(e2e_step, max(2, args.steps // 2), 2, world, gpu)
+    e2e_ms, _ = timed_steps(e2e_step, max(2, args.steps // 2), 3, world, gpu)
     out_h.clear()
     del Ah, Bh
     es = A_sh.element_size()

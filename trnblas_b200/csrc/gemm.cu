@@ -220,7 +220,9 @@ int group_m_override() {
 // power cap (one-CTA kernel, band of 16 row tiles): DRAM reads per launch
 // 144 -> 69 GB; the same box went 1145 -> 1209 TFLOP/s (pair kernel:
 // 912 -> 1347 TFLOP/s on another box).
-// TRNBLAS_B200_GEMM_WAVESYNC = 0 / 1 overrides the default (on).
+// TRNBLAS_B200_GEMM_WAVESYNC = 0 / 1 overrides the default (on). Not used
+// for a triangular operand (trmm), whose tiles' K ranges differ: the CTAs of
+// a wave would wait for its longest tile.
 bool use_wave_sync(long long K, long long tiles, long long grid) {
   static const int mode = [] {
     const char* s = std::getenv("TRNBLAS_B200_GEMM_WAVESYNC");
@@ -243,7 +245,7 @@ int launch_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int grid = static_cast<int>(std::min<long long>(p.num_tiles, num_sms()));
-  if (p.mode == kModeGemm && use_wave_sync(p.K, p.num_tiles, grid)) p.wave_ctr = wave_counter(stream);
+  if (p.mode == kModeGemm && !p.tri && use_wave_sync(p.K, p.num_tiles, grid)) p.wave_ctr = wave_counter(stream);
   kern<<<grid, Cfg::THREADS, smem, stream>>>(a0, a1, b0, b1, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
@@ -288,7 +290,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& a1, const CUtensor
   }
   const int pairs = static_cast<int>(std::min<long long>(p.num_tiles, max_pairs[dev]));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  if (use_wave_sync(p.K, p.num_tiles, pairs)) p.wave_ctr = wave_counter(stream);
+  if (!p.tri && use_wave_sync(p.K, p.num_tiles, pairs)) p.wave_ctr = wave_counter(stream);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, a1, b, b1, p);
   if (e != cudaSuccess) return cuda_fail(e, "pair gemm kernel launch");
   return TRNBLAS_OK;

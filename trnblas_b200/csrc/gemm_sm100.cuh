@@ -329,6 +329,11 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& bz,
   const int rr = r - g * band;
   mb = first_m + rr % gsz;
   nb = rr / gsz;
+  // triangular operand: the tiles with the longest K ranges first (rows from
+  // the bottom for a lower op(A), columns from the right for an op(B) whose
+  // range ends at its columns), so that the walk ends on short tiles
+  if (p.tri == 1) mb = p.tiles_m - 1 - mb;
+  if (p.tri == 4) nb = p.tiles_n - 1 - nb;
   if (p.ready) {
     bz = (bz + p.rot_b) % p.batch;
     mb = (mb + p.rot_m) % p.tiles_m;

@@ -580,7 +580,8 @@ def run_pair(args, rank, world, gpu, nocc, nvir, naux, steps=None, warmup=None):
             out["e2e"] = tp.pair_energy(Bh, eoh, evh)
 
     e2e_ms, _ = timed_steps(e2e_step, max(1, min(steps, 2)), 1, world, gpu)
-    e2e_info = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(Bh.numel() * 4 * world),
+    # at N > 1 each rank uploads a 1/N slice of B and an all-gather shares them
+    e2e_info = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(Bh.numel() * 4),
                 "d2h_bytes_per_step": 8 * world,
                 "path": "trnblas_b200.batched_pair_energy / parallel.pair_energy on pinned host B"}
     del Bh

@@ -75,6 +75,8 @@ def _worker(rank, world, port, q):
         ref = PE.chunked_energy(Bh.numpy(), eo.numpy(), ev.numpy())
         out["energy"] = abs(E - ref) <= 1e-9 * abs(ref)
         out["E"] = E
+        # host B: each rank uploads a slice, an all-gather assembles it
+        out["energy_host"] = tp.pair_energy(Bh.pin_memory(), eo, ev) == E
         import numpy as np
 
         d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "dfmp2.npz"))

@@ -497,19 +497,38 @@ def gemm_2d(
 # ── DF-MP2 pair energy ───────────────────────────────────────────────────────
 
 
+def _replicate_host_rows(x: torch.Tensor, group=None) -> torch.Tensor:
+    """A host tensor that every rank needs whole on its device: rank r copies
+    rows [r q, (r + 1) q) (q = ceil(rows / w)) to its device and one
+    all-gather assembles all rows on every rank, so the host links carry the
+    tensor once in all instead of once per rank (the ranks' uploads share the
+    host's memory bandwidth; NVLink carries the rest)."""
+    r, w = _rank_world(group)
+    n = x.shape[0]
+    q = -(-n // w)
+    part = torch.zeros((q, *x.shape[1:]), dtype=x.dtype, device=device())
+    r0, r1 = min(r * q, n), min((r + 1) * q, n)
+    if r1 > r0:
+        part[: r1 - r0].copy_(x[r0:r1], non_blocking=True)
+    return all_gather_rows(part, group)[:n]
+
+
 def pair_energy(
     B_full: torch.Tensor, eps_occ: torch.Tensor, eps_vir: torch.Tensor, group=None
 ) -> float:
     """MP2 pair energy with the occupied pairs split over the ranks.
 
     `B_full` (nocc, nvir, naux) is on this rank's device on every rank, as in
-    the reference (trnblas/parallel.py:126-162). Rank r computes the r-th
+    the reference (trnblas/parallel.py:126-162); a host `B_full` (the same
+    on every rank) is uploaded a 1/w slice per rank and all-gathered. Rank r computes the r-th
     pair-count-balanced range of the i <= j pair list on the fused kernel;
     one all-reduce of an fp64 scalar sums them (fp64: the kernel's 1e-9
     relative accuracy would not survive an fp32 sum). Returns a float on
     every rank.
     """
     r, w = _rank_world(group) if _distributed() else (0, 1)
+    if w > 1 and B_full.device.type == "cpu":
+        B_full = _replicate_host_rows(B_full, group)
     nocc = B_full.shape[0]
     p0, p1 = _energy.pair_ranges(nocc, w)[r]
     if _local_energy is not None:
